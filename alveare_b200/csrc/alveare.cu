@@ -1,0 +1,763 @@
+// Host side of the C ABI declared in include/alveare_b200.h: context, scratch
+// arena, weight registry (load-time repack), kernel launchers.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <climits>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <set>
+#include <string>
+#include <vector>
+
+#include "../../include/alveare_b200.h"
+#include "kernels.cuh"
+
+using namespace alv;
+
+namespace {
+
+constexpr int kVersion = 100;             // 0.1.0
+constexpr uint32_t kMaxCounters = 65536;  // row tiles per matrix (N <= 1,048,576)
+constexpr size_t kHeaderBytes = 1024;     // status word + grid barrier
+constexpr size_t kMaxSmem = 227 * 1024;
+
+struct Mat {
+  uint8_t* dev = nullptr;
+  Q4Mat m{};
+  uint32_t rows = 0, cols = 0;
+  size_t bytes = 0;
+};
+
+struct Weight {
+  int kind = 0;  // 1 gemv, 2 ffn
+  Mat a, b;      // gemv: a; ffn: a = gate/up interleaved, b = down
+  uint32_t H = 0, I = 0, i_begin = 0, i_end = 0;
+  int act = 0;
+};
+
+}  // namespace
+
+struct alv_ctx {
+  int device = 0;
+  int num_sms = 0;
+  std::string err;
+  std::vector<std::unique_ptr<Weight>> weights;  // handle = index + 1
+  uint8_t* scratch = nullptr;                    // [header][counters][work]
+  size_t scratch_bytes = 0;
+  void* io = nullptr;                            // device staging for host-buffer calls
+  size_t io_bytes = 0;
+  cudaStream_t stream = nullptr;                 // internal stream (loads, host calls)
+};
+
+namespace {
+
+int fail(alv_ctx* ctx, int code, const std::string& msg) {
+  if (ctx) ctx->err = msg;
+  return code;
+}
+
+#define ALV_CUDA(ctx, call)                                                              \
+  do {                                                                                   \
+    cudaError_t e_ = (call);                                                             \
+    if (e_ != cudaSuccess)                                                               \
+      return fail((ctx), ALV_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+int set_device(alv_ctx* ctx) {
+  ALV_CUDA(ctx, cudaSetDevice(ctx->device));
+  return ALV_OK;
+}
+
+uint32_t* status_ptr(alv_ctx* ctx) { return reinterpret_cast<uint32_t*>(ctx->scratch); }
+GridBar* bar_ptr(alv_ctx* ctx) { return reinterpret_cast<GridBar*>(ctx->scratch + 256); }
+uint32_t* counters_ptr(alv_ctx* ctx) { return reinterpret_cast<uint32_t*>(ctx->scratch + kHeaderBytes); }
+uint8_t* work_ptr(alv_ctx* ctx) {
+  return ctx->scratch + kHeaderBytes + static_cast<size_t>(kMaxCounters) * 4;
+}
+
+// The scratch arena: header and counters keep their offsets forever (counters
+// are only ever counters and are zero between launches); the work area above
+// them is re-laid out per call.
+int ensure_scratch(alv_ctx* ctx, size_t work_bytes) {
+  const size_t need = kHeaderBytes + static_cast<size_t>(kMaxCounters) * 4 + work_bytes;
+  if (ctx->scratch && ctx->scratch_bytes >= need) return ALV_OK;
+  ALV_CUDA(ctx, cudaDeviceSynchronize());
+  if (ctx->scratch) ALV_CUDA(ctx, cudaFree(ctx->scratch));
+  ctx->scratch = nullptr;
+  const size_t bytes = std::max(need, static_cast<size_t>(8) << 20);
+  ALV_CUDA(ctx, cudaMalloc(&ctx->scratch, bytes));
+  ALV_CUDA(ctx, cudaMemset(ctx->scratch, 0, bytes));
+  ctx->scratch_bytes = bytes;
+  return ALV_OK;
+}
+
+Weight* get_weight(alv_ctx* ctx, alv_handle h, int kind) {
+  if (h == 0 || h > ctx->weights.size()) return nullptr;
+  Weight* w = ctx->weights[h - 1].get();
+  if (!w || (kind && w->kind != kind)) return nullptr;
+  return w;
+}
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+uint32_t pow2_ceil(uint32_t v) {
+  uint32_t p = 1;
+  while (p < v) p <<= 1;
+  return p;
+}
+
+// Survey the scales of the blocks that will be repacked: the fast dequant
+// path needs every nonzero scale finite and the scale exponents within a
+// window of 120 binades (je = emax + 6 <= emin + 126).
+struct Survey {
+  int fast = 0;
+  int je = 0;
+};
+
+int survey_mat(alv_ctx* ctx, const RepackSrc& s, Survey* out) {
+  int* info = nullptr;
+  ALV_CUDA(ctx, cudaMalloc(&info, 3 * sizeof(int)));
+  const int init[3] = {INT_MIN, INT_MAX, 0};
+  ALV_CUDA(ctx, cudaMemcpyAsync(info, init, sizeof(init), cudaMemcpyHostToDevice, ctx->stream));
+  const uint64_t nblk = static_cast<uint64_t>(s.RT) * 16 * (s.K / 32);
+  if (nblk) {
+    q4_scale_survey_kernel<<<static_cast<unsigned>((nblk + 255) / 256), 256, 0, ctx->stream>>>(s, info);
+    ALV_CUDA(ctx, cudaGetLastError());
+  }
+  int h[3];
+  ALV_CUDA(ctx, cudaMemcpyAsync(h, info, sizeof(h), cudaMemcpyDeviceToHost, ctx->stream));
+  ALV_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  ALV_CUDA(ctx, cudaFree(info));
+  Survey r;
+  if (!h[2]) {
+    if (h[0] == INT_MIN) {
+      r.fast = 1;  // no block with a nonzero q: every stored scale is 0
+    } else {
+      r.je = h[0] + 6;
+      r.fast = (r.je <= h[1] + 126) && r.je >= -126 && r.je <= 127;
+      if (!r.fast) r.je = 0;
+    }
+  }
+  *out = r;
+  return ALV_OK;
+}
+
+// Repack into a new device buffer with the chosen dequant path.
+int repack_mat(alv_ctx* ctx, const RepackSrc& s, const Survey& sv, uint32_t rows, uint32_t cols, Mat* out) {
+  const uint64_t nunits = static_cast<uint64_t>(s.RT) * s.KT;
+  Mat m;
+  m.bytes = nunits * kUnitBytes;
+  ALV_CUDA(ctx, cudaMalloc(&m.dev, std::max<size_t>(m.bytes, 16)));
+  if (nunits) {
+    const uint64_t nwords = nunits * 144;
+    q4_repack_kernel<<<static_cast<unsigned>((nwords + 255) / 256), 256, 0, ctx->stream>>>(
+        s, sv.fast, sv.je, reinterpret_cast<uint32_t*>(m.dev));
+    ALV_CUDA(ctx, cudaGetLastError());
+  }
+  ALV_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  m.m.units = m.dev;
+  m.m.RT = s.RT;
+  m.m.KT = s.KT;
+  m.m.fast = static_cast<uint32_t>(sv.fast);
+  m.m.scale_mul = sv.fast ? ldexpf(1.0f, sv.je) : 1.0f;
+  m.rows = rows;
+  m.cols = cols;
+  *out = m;
+  return ALV_OK;
+}
+
+int build_mat(alv_ctx* ctx, const RepackSrc& s, uint32_t rows, uint32_t cols, Mat* out) {
+  Survey sv;
+  int rc = survey_mat(ctx, s, &sv);
+  if (rc) return rc;
+  return repack_mat(ctx, s, sv, rows, cols, out);
+}
+
+// Copy a host source buffer to the device (or use the device pointer).
+int stage_source(alv_ctx* ctx, const void* src, size_t bytes, int on_device, const uint8_t** dev,
+                 uint8_t** owned) {
+  *owned = nullptr;
+  if (on_device) {
+    *dev = static_cast<const uint8_t*>(src);
+    return ALV_OK;
+  }
+  uint8_t* d = nullptr;
+  ALV_CUDA(ctx, cudaMalloc(&d, std::max<size_t>(bytes, 16)));
+  ALV_CUDA(ctx, cudaMemcpy(d, src, bytes, cudaMemcpyHostToDevice));
+  *dev = d;
+  *owned = d;
+  return ALV_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Launchers
+// ---------------------------------------------------------------------------
+// Raise the kernel's dynamic shared-memory limit once per (kernel, device) to
+// the maximum, so launches need no per-call attribute changes.
+template <class K>
+int prepare_kernel(alv_ctx* ctx, K kernel, size_t smem) {
+  if (smem > kMaxSmem)
+    return fail(ctx, ALV_ERR_UNSUPPORTED, "problem needs " + std::to_string(smem) +
+                                              " B of shared memory (max " + std::to_string(kMaxSmem) + ")");
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  const auto key = std::make_pair(reinterpret_cast<const void*>(kernel), ctx->device);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!done.count(key)) {
+    ALV_CUDA(ctx, cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(kMaxSmem)));
+    done.insert(key);
+  }
+  return ALV_OK;
+}
+
+// Ring stages per warp that fit beside `other` bytes of shared memory (max 4).
+uint32_t ring_stages(size_t other) {
+  for (uint32_t nst = 4; nst >= 1; --nst)
+    if (ring_smem_bytes(nst) + other <= kMaxSmem) return nst;
+  return 0;
+}
+
+template <int NCOLS, bool SPLIT, bool FAST>
+int launch_gemv_t(alv_ctx* ctx, GemvParams p, cudaStream_t st) {
+  const size_t xs = frag_bytes(p.m.KT, NCOLS);
+  p.nst = ring_stages(xs);
+  if (!p.nst) return fail(ctx, ALV_ERR_UNSUPPORTED, "gemv: K too large for the shared-memory fragment stage");
+  const size_t smem = ring_smem_bytes(p.nst) + xs;
+  auto k = gemv_kernel<NCOLS, SPLIT, FAST>;
+  int rc = prepare_kernel(ctx, k, smem);
+  if (rc) return rc;
+  k<<<ctx->num_sms, kWarpsPerCta * 32, smem, st>>>(p);
+  ALV_CUDA(ctx, cudaGetLastError());
+  return ALV_OK;
+}
+
+template <bool FAST>
+int launch_gemv_f(alv_ctx* ctx, const GemvParams& p, bool split, uint32_t ncols, cudaStream_t st) {
+  if (split) {
+    switch (ncols) {
+      case 2: return launch_gemv_t<2, true, FAST>(ctx, p, st);
+      case 4: return launch_gemv_t<4, true, FAST>(ctx, p, st);
+      case 8: return launch_gemv_t<8, true, FAST>(ctx, p, st);
+      case 16: return launch_gemv_t<16, true, FAST>(ctx, p, st);
+    }
+  } else {
+    switch (ncols) {
+      case 1: return launch_gemv_t<1, false, FAST>(ctx, p, st);
+      case 2: return launch_gemv_t<2, false, FAST>(ctx, p, st);
+      case 4: return launch_gemv_t<4, false, FAST>(ctx, p, st);
+      case 8: return launch_gemv_t<8, false, FAST>(ctx, p, st);
+      case 16: return launch_gemv_t<16, false, FAST>(ctx, p, st);
+    }
+  }
+  return fail(ctx, ALV_ERR_UNSUPPORTED, "unsupported column count");
+}
+
+int launch_gemv(alv_ctx* ctx, const GemvParams& p, bool split, uint32_t ncols, cudaStream_t st) {
+  return p.m.fast ? launch_gemv_f<true>(ctx, p, split, ncols, st) : launch_gemv_f<false>(ctx, p, split, ncols, st);
+}
+
+template <int NT, bool SPLIT, bool FAST>
+int launch_ffn_t(alv_ctx* ctx, FfnParams p, cudaStream_t st) {
+  constexpr int NCA = SPLIT ? 2 * NT : NT;
+  size_t other = std::max(frag_bytes(p.gu.KT, NCA), frag_bytes(p.dn.KT, NT)) + 32 * sizeof(float);
+  if (p.glue) other += static_cast<size_t>(p.ntok) * p.H * sizeof(float);
+  p.nst = ring_stages(other);
+  if (!p.nst) return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn: H or I too large for the shared-memory fragment stage");
+  const size_t smem = ring_smem_bytes(p.nst) + other;
+  auto k = ffn_kernel<NT, SPLIT, FAST>;
+  int rc = prepare_kernel(ctx, k, smem);
+  if (rc) return rc;
+  k<<<ctx->num_sms, kWarpsPerCta * 32, smem, st>>>(p);
+  ALV_CUDA(ctx, cudaGetLastError());
+  return ALV_OK;
+}
+
+template <bool FAST>
+int launch_ffn_f(alv_ctx* ctx, const FfnParams& p, bool split, uint32_t nt, cudaStream_t st) {
+  if (split) {
+    switch (nt) {
+      case 1: return launch_ffn_t<1, true, FAST>(ctx, p, st);
+      case 2: return launch_ffn_t<2, true, FAST>(ctx, p, st);
+      case 4: return launch_ffn_t<4, true, FAST>(ctx, p, st);
+      case 8: return launch_ffn_t<8, true, FAST>(ctx, p, st);
+    }
+  } else {
+    switch (nt) {
+      case 1: return launch_ffn_t<1, false, FAST>(ctx, p, st);
+      case 2: return launch_ffn_t<2, false, FAST>(ctx, p, st);
+      case 4: return launch_ffn_t<4, false, FAST>(ctx, p, st);
+      case 8: return launch_ffn_t<8, false, FAST>(ctx, p, st);
+    }
+  }
+  return fail(ctx, ALV_ERR_UNSUPPORTED, "unsupported token count");
+}
+
+// Both FFN matrices were repacked for the same dequant path.
+int launch_ffn(alv_ctx* ctx, const FfnParams& p, bool split, uint32_t nt, cudaStream_t st) {
+  return p.gu.fast ? launch_ffn_f<true>(ctx, p, split, nt, st) : launch_ffn_f<false>(ctx, p, split, nt, st);
+}
+
+size_t ws_floats(alv_ctx* ctx, const Q4Mat& m, int ntok) {
+  const uint64_t U = static_cast<uint64_t>(m.RT) * m.KT;
+  const uint64_t W = effective_warps(static_cast<uint64_t>(ctx->num_sms) * kWarpsPerCta, U, m.KT);
+  return static_cast<size_t>(W) * 2 * ntok * 16;
+}
+
+bool valid_dtype(int d) { return d == ALV_F32 || d == ALV_BF16; }
+
+int do_gemv(alv_ctx* ctx, Weight* w, int ntok, const void* x, int x_dtype, void* y, int y_dtype,
+            cudaStream_t st) {
+  const bool split = x_dtype == ALV_F32;
+  const uint32_t ncols = pow2_ceil(static_cast<uint32_t>(split ? 2 * ntok : ntok));
+  if (ntok < 1 || ncols > 16)
+    return fail(ctx, ALV_ERR_UNSUPPORTED, "gemv: ntok must be 1..16 (bf16 x) or 1..8 (fp32 x)");
+  if (w->a.m.RT > kMaxCounters) return fail(ctx, ALV_ERR_UNSUPPORTED, "gemv: too many rows");
+  const size_t ws_bytes = align_up(ws_floats(ctx, w->a.m, ntok) * 4, 256);
+  int rc = ensure_scratch(ctx, ws_bytes);
+  if (rc) return rc;
+  GemvParams p{};
+  p.m = w->a.m;
+  p.x = XSrc{x, x_dtype == ALV_BF16, ntok, w->a.cols, w->a.cols};
+  p.epi = RowsEpi{y_dtype == ALV_F32 ? static_cast<float*>(y) : nullptr,
+                  y_dtype == ALV_BF16 ? static_cast<uint16_t*>(y) : nullptr, w->a.rows, w->a.rows,
+                  w->a.m.scale_mul};
+  p.fx = Fixup{reinterpret_cast<float*>(work_ptr(ctx)), counters_ptr(ctx)};
+  p.status = status_ptr(ctx);
+  return launch_gemv(ctx, p, split, ncols, st);
+}
+
+struct FfnIo {
+  const void* x = nullptr;
+  int x_dtype = ALV_F32;
+  int glue = 0;
+  const uint16_t* x_in = nullptr;
+  const float* down_in = nullptr;
+  uint16_t* x_out = nullptr;
+  float* y32 = nullptr;
+  uint16_t* y16 = nullptr;
+};
+
+int do_ffn(alv_ctx* ctx, Weight* w, int ntok, const FfnIo& io, cudaStream_t st) {
+  if (ntok < 1 || ntok > 8) return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn: ntok must be 1..8");
+  const bool split = !io.glue && io.x_dtype == ALV_F32;
+  const uint32_t nt = pow2_ceil(static_cast<uint32_t>(ntok));
+  if (w->a.m.RT + w->b.m.RT > kMaxCounters) return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn: too large");
+  const uint32_t act_ld = static_cast<uint32_t>(align_up(w->I, 64));
+  const size_t wsA = align_up(ws_floats(ctx, w->a.m, ntok) * 4, 256);
+  const size_t wsB = align_up(ws_floats(ctx, w->b.m, ntok) * 4, 256);
+  const size_t actb = align_up(static_cast<size_t>(ntok) * act_ld * 2, 256);
+  int rc = ensure_scratch(ctx, wsA + wsB + actb);
+  if (rc) return rc;
+  uint8_t* wk = work_ptr(ctx);
+  FfnParams p{};
+  p.gu = w->a.m;
+  p.dn = w->b.m;
+  p.H = w->H;
+  p.I = w->i_end - w->i_begin;
+  p.fn = w->act;
+  p.ntok = ntok;
+  p.x = XSrc{io.x, io.x_dtype == ALV_BF16, ntok, w->H, w->H};
+  p.glue = io.glue;
+  p.x_in = io.x_in;
+  p.down_in = io.down_in;
+  p.x_out = io.x_out;
+  p.eps = 1e-6f;
+  p.out = RowsEpi{io.y32, io.y16, w->H, w->H, w->b.m.scale_mul};
+  p.act = reinterpret_cast<uint16_t*>(wk + wsA + wsB);
+  p.act_ld = act_ld;
+  p.fxA = Fixup{reinterpret_cast<float*>(wk), counters_ptr(ctx)};
+  p.fxB = Fixup{reinterpret_cast<float*>(wk + wsA), counters_ptr(ctx) + w->a.m.RT};
+  p.bar = bar_ptr(ctx);
+  p.status = status_ptr(ctx);
+  return launch_ffn(ctx, p, split, nt, st);
+}
+
+int io_buffers(alv_ctx* ctx, size_t bytes) {
+  if (ctx->io && ctx->io_bytes >= bytes) return ALV_OK;
+  if (ctx->io) ALV_CUDA(ctx, cudaFree(ctx->io));
+  ctx->io = nullptr;
+  ALV_CUDA(ctx, cudaMalloc(&ctx->io, bytes));
+  ctx->io_bytes = bytes;
+  return ALV_OK;
+}
+
+int check_status(alv_ctx* ctx, cudaStream_t st) {
+  ALV_CUDA(ctx, cudaStreamSynchronize(st));
+  if (!ctx->scratch) return ALV_OK;
+  uint32_t s = 0;
+  ALV_CUDA(ctx, cudaMemcpy(&s, status_ptr(ctx), sizeof(s), cudaMemcpyDeviceToHost));
+  if (s) {
+    // A kernel gave up mid-way: clear status, barrier and counters.
+    ALV_CUDA(ctx, cudaMemset(ctx->scratch, 0, kHeaderBytes + static_cast<size_t>(kMaxCounters) * 4));
+    char buf[128];
+    std::snprintf(buf, sizeof(buf), "device-side wait timed out (status 0x%x)", s);
+    return fail(ctx, ALV_ERR_TIMEOUT, buf);
+  }
+  return ALV_OK;
+}
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" {
+
+int alv_version(void) { return kVersion; }
+
+int alv_ctx_create(int device, alv_ctx** out) {
+  if (!out) return ALV_ERR_ARG;
+  *out = nullptr;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return ALV_ERR_NO_DEVICE;
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return ALV_ERR_NO_DEVICE;
+  if (prop.major != 10) return ALV_ERR_NO_DEVICE;  // built for sm_100a only
+  auto* ctx = new alv_ctx();
+  ctx->device = device;
+  ctx->num_sms = prop.multiProcessorCount;
+  if (cudaSetDevice(device) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess) {
+    delete ctx;
+    return ALV_ERR_CUDA;
+  }
+  if (ensure_scratch(ctx, 0) != ALV_OK) {
+    cudaStreamDestroy(ctx->stream);
+    delete ctx;
+    return ALV_ERR_CUDA;
+  }
+  *out = ctx;
+  return ALV_OK;
+}
+
+int alv_ctx_destroy(alv_ctx* ctx) {
+  if (!ctx) return ALV_ERR_ARG;
+  cudaSetDevice(ctx->device);
+  cudaDeviceSynchronize();
+  for (auto& w : ctx->weights) {
+    if (!w) continue;
+    cudaFree(w->a.dev);
+    cudaFree(w->b.dev);
+  }
+  cudaFree(ctx->scratch);
+  cudaFree(ctx->io);
+  cudaStreamDestroy(ctx->stream);
+  delete ctx;
+  return ALV_OK;
+}
+
+const char* alv_last_error(const alv_ctx* ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+
+int alv_sync_status(alv_ctx* ctx, void* stream) {
+  if (!ctx) return ALV_ERR_ARG;
+  int rc = set_device(ctx);
+  if (rc) return rc;
+  return check_status(ctx, static_cast<cudaStream_t>(stream));
+}
+
+int alv_q4_quantize(alv_ctx* ctx, const float* w, int N, int K, uint8_t* combined, void* stream) {
+  if (!ctx || !w || !combined || N < 0 || K < 0) return fail(ctx, ALV_ERR_ARG, "q4_quantize: bad argument");
+  if (K % 32) return fail(ctx, ALV_ERR_SHAPE, "q4_quantize: K must be a multiple of 32");
+  int rc = set_device(ctx);
+  if (rc) return rc;
+  const size_t n = static_cast<size_t>(N) * (K / 32);
+  if (n == 0) return ALV_OK;
+  q4_quantize_kernel<<<static_cast<unsigned>((n + 127) / 128), 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      w, N, K, combined);
+  ALV_CUDA(ctx, cudaGetLastError());
+  return ALV_OK;
+}
+
+int alv_gemv_weight_create(alv_ctx* ctx, int N, int K, const void* combined, size_t nbytes,
+                           int on_device, alv_handle* out) {
+  if (!ctx || !combined || !out || N <= 0 || K <= 0) return fail(ctx, ALV_ERR_ARG, "gemv_weight_create: bad argument");
+  if (K % 32) return fail(ctx, ALV_ERR_SHAPE, "gemv_weight_create: K must be a multiple of 32");
+  const size_t expect = static_cast<size_t>(N) * (K / 32) * 20;
+  if (nbytes != expect)
+    return fail(ctx, ALV_ERR_SHAPE, "gemv_weight_create: expected " + std::to_string(expect) + " bytes, got " +
+                                        std::to_string(nbytes));
+  int rc = set_device(ctx);
+  if (rc) return rc;
+  const uint8_t* src = nullptr;
+  uint8_t* owned = nullptr;
+  rc = stage_source(ctx, combined, nbytes, on_device, &src, &owned);
+  if (rc) return rc;
+  RepackSrc s{};
+  s.a = src;
+  s.b = nullptr;
+  s.rows = static_cast<uint32_t>(N);
+  s.row_off = 0;
+  s.row_bytes = static_cast<uint64_t>(K / 32) * 20;
+  s.blk_off = 0;
+  s.K = static_cast<uint32_t>(K);
+  s.interleave8 = 0;
+  s.RT = static_cast<uint32_t>((N + 15) / 16);
+  s.KT = static_cast<uint32_t>((K + 63) / 64);
+  auto w = std::make_unique<Weight>();
+  w->kind = 1;
+  rc = build_mat(ctx, s, static_cast<uint32_t>(N), static_cast<uint32_t>(K), &w->a);
+  if (owned) cudaFree(owned);
+  if (rc) return rc;
+  ctx->weights.push_back(std::move(w));
+  *out = static_cast<alv_handle>(ctx->weights.size());
+  return ALV_OK;
+}
+
+int alv_ffn_weight_create(alv_ctx* ctx, int H, int I, int act, const void* gate, const void* up,
+                          const void* down, int on_device, int i_begin, int i_end, alv_handle* out) {
+  if (!ctx || !gate || !up || !down || !out || H <= 0 || I <= 0)
+    return fail(ctx, ALV_ERR_ARG, "ffn_weight_create: bad argument");
+  if (act != ALV_ACT_GELU && act != ALV_ACT_SILU) return fail(ctx, ALV_ERR_ARG, "ffn_weight_create: bad activation");
+  if (H % 32 || I % 32) return fail(ctx, ALV_ERR_SHAPE, "ffn_weight_create: H and I must be multiples of 32");
+  if (i_begin < 0 || i_end > I || i_begin >= i_end || i_begin % 32 || i_end % 32)
+    return fail(ctx, ALV_ERR_SHAPE, "ffn_weight_create: slice must be 32-aligned inside [0, I)");
+  int rc = set_device(ctx);
+  if (rc) return rc;
+  const size_t gu_bytes = static_cast<size_t>(I) * (H / 32) * 20;
+  const size_t dn_bytes = static_cast<size_t>(H) * (I / 32) * 20;
+  const uint8_t *g = nullptr, *u = nullptr, *d = nullptr;
+  uint8_t *og = nullptr, *ou = nullptr, *od = nullptr;
+  if ((rc = stage_source(ctx, gate, gu_bytes, on_device, &g, &og)) ||
+      (rc = stage_source(ctx, up, gu_bytes, on_device, &u, &ou)) ||
+      (rc = stage_source(ctx, down, dn_bytes, on_device, &d, &od))) {
+    cudaFree(og);
+    cudaFree(ou);
+    cudaFree(od);
+    return rc;
+  }
+  const uint32_t Il = static_cast<uint32_t>(i_end - i_begin);
+  auto w = std::make_unique<Weight>();
+  w->kind = 2;
+  w->H = static_cast<uint32_t>(H);
+  w->I = static_cast<uint32_t>(I);
+  w->i_begin = static_cast<uint32_t>(i_begin);
+  w->i_end = static_cast<uint32_t>(i_end);
+  w->act = act;
+  RepackSrc sa{};
+  sa.a = g;
+  sa.b = u;
+  sa.rows = Il;
+  sa.row_off = static_cast<uint32_t>(i_begin);
+  sa.row_bytes = static_cast<uint64_t>(H / 32) * 20;
+  sa.blk_off = 0;
+  sa.K = static_cast<uint32_t>(H);
+  sa.interleave8 = 1;
+  sa.RT = (Il + 7) / 8;
+  sa.KT = static_cast<uint32_t>((H + 63) / 64);
+  RepackSrc sb{};
+  sb.a = d;
+  sb.b = nullptr;
+  sb.rows = static_cast<uint32_t>(H);
+  sb.row_off = 0;
+  sb.row_bytes = static_cast<uint64_t>(I / 32) * 20;
+  sb.blk_off = static_cast<uint32_t>(i_begin / 32);
+  sb.K = Il;
+  sb.interleave8 = 0;
+  sb.RT = static_cast<uint32_t>((H + 15) / 16);
+  sb.KT = (Il + 63) / 64;
+  // One kernel dequantizes both matrices: they share the dequant path.
+  Survey sva, svb;
+  if (!(rc = survey_mat(ctx, sa, &sva)) && !(rc = survey_mat(ctx, sb, &svb))) {
+    if (!(sva.fast && svb.fast)) sva = svb = Survey{};
+    rc = repack_mat(ctx, sa, sva, Il, static_cast<uint32_t>(H), &w->a);
+    if (!rc) rc = repack_mat(ctx, sb, svb, static_cast<uint32_t>(H), Il, &w->b);
+  }
+  cudaFree(og);
+  cudaFree(ou);
+  cudaFree(od);
+  if (rc) {
+    cudaFree(w->a.dev);
+    cudaFree(w->b.dev);
+    return rc;
+  }
+  ctx->weights.push_back(std::move(w));
+  *out = static_cast<alv_handle>(ctx->weights.size());
+  return ALV_OK;
+}
+
+int alv_weight_destroy(alv_ctx* ctx, alv_handle h) {
+  if (!ctx) return ALV_ERR_ARG;
+  Weight* w = get_weight(ctx, h, 0);
+  if (!w) return fail(ctx, ALV_ERR_HANDLE, "weight_destroy: invalid handle");
+  int rc = set_device(ctx);
+  if (rc) return rc;
+  ALV_CUDA(ctx, cudaDeviceSynchronize());
+  cudaFree(w->a.dev);
+  cudaFree(w->b.dev);
+  ctx->weights[h - 1].reset();
+  return ALV_OK;
+}
+
+int alv_ffn_set_activation(alv_ctx* ctx, alv_handle h, int act) {
+  if (!ctx) return ALV_ERR_ARG;
+  if (act != ALV_ACT_GELU && act != ALV_ACT_SILU) return fail(ctx, ALV_ERR_ARG, "ffn_set_activation: bad activation");
+  Weight* w = get_weight(ctx, h, 2);
+  if (!w) return fail(ctx, ALV_ERR_HANDLE, "ffn_set_activation: invalid handle (not an ffn weight)");
+  w->act = act;
+  return ALV_OK;
+}
+
+int alv_weight_info(alv_ctx* ctx, alv_handle h, int64_t* info) {
+  if (!ctx || !info) return ALV_ERR_ARG;
+  Weight* w = get_weight(ctx, h, 0);
+  if (!w) return fail(ctx, ALV_ERR_HANDLE, "weight_info: invalid handle");
+  info[0] = w->kind;
+  info[1] = w->kind == 1 ? w->a.rows : w->H;
+  info[2] = w->kind == 1 ? w->a.cols : (w->i_end - w->i_begin);
+  info[3] = w->a.m.fast;
+  info[4] = w->kind == 2 ? w->b.m.fast : 0;
+  info[5] = static_cast<int64_t>(w->a.bytes + w->b.bytes);
+  info[6] = w->i_begin;
+  info[7] = w->i_end;
+  return ALV_OK;
+}
+
+int alv_weight_dequantize(alv_ctx* ctx, alv_handle h, int which, uint16_t* out, void* stream) {
+  if (!ctx || !out) return fail(ctx, ALV_ERR_ARG, "weight_dequantize: bad argument");
+  Weight* w = get_weight(ctx, h, 0);
+  if (!w) return fail(ctx, ALV_ERR_HANDLE, "weight_dequantize: invalid handle");
+  int rc = set_device(ctx);
+  if (rc) return rc;
+  const Mat* m = nullptr;
+  uint32_t rows = 0, K = 0;
+  if (w->kind == 1) {
+    if (which != 0) return fail(ctx, ALV_ERR_ARG, "weight_dequantize: gemv weights have one matrix");
+    m = &w->a;
+    rows = m->rows;
+    K = m->cols;
+  } else {
+    if (which < 0 || which > 2) return fail(ctx, ALV_ERR_ARG, "weight_dequantize: which must be 0..2");
+    m = which == 2 ? &w->b : &w->a;
+    rows = which == 2 ? w->H : (w->i_end - w->i_begin);
+    K = which == 2 ? (w->i_end - w->i_begin) : w->H;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const uint64_t nthreads = static_cast<uint64_t>(m->m.RT) * m->m.KT * 32;
+  if (w->kind == 2 && which < 2) {
+    // gate/up live interleaved: dequantize the whole interleaved matrix into a
+    // temporary (2*I rows) and gather the requested half.
+    const uint32_t rows_all = m->m.RT * 16;
+    uint16_t* tmp = nullptr;
+    ALV_CUDA(ctx, cudaMalloc(&tmp, static_cast<size_t>(rows_all) * K * 2));
+    q4_dequant_kernel<<<static_cast<unsigned>((nthreads + 255) / 256), 256, 0, st>>>(m->m, rows_all, K, tmp);
+    ALV_CUDA(ctx, cudaGetLastError());
+    for (uint32_t i = 0; i < rows; ++i) {
+      const uint32_t src_row = (i / 8) * 16 + (i % 8) + (which == 1 ? 8 : 0);
+      ALV_CUDA(ctx, cudaMemcpyAsync(out + static_cast<size_t>(i) * K, tmp + static_cast<size_t>(src_row) * K,
+                                    static_cast<size_t>(K) * 2, cudaMemcpyDeviceToDevice, st));
+    }
+    ALV_CUDA(ctx, cudaStreamSynchronize(st));
+    ALV_CUDA(ctx, cudaFree(tmp));
+    return ALV_OK;
+  }
+  if (nthreads) {
+    q4_dequant_kernel<<<static_cast<unsigned>((nthreads + 255) / 256), 256, 0, st>>>(m->m, rows, K, out);
+    ALV_CUDA(ctx, cudaGetLastError());
+  }
+  return ALV_OK;
+}
+
+int alv_gemv(alv_ctx* ctx, alv_handle h, int ntok, const void* x, int x_dtype, void* y, int y_dtype,
+             void* stream) {
+  if (!ctx || !x || !y || !valid_dtype(x_dtype) || !valid_dtype(y_dtype))
+    return fail(ctx, ALV_ERR_ARG, "gemv: bad argument");
+  Weight* w = get_weight(ctx, h, 1);
+  if (!w) return fail(ctx, ALV_ERR_HANDLE, "gemv: invalid handle (not a gemv weight)");
+  int rc = set_device(ctx);
+  if (rc) return rc;
+  return do_gemv(ctx, w, ntok, x, x_dtype, y, y_dtype, static_cast<cudaStream_t>(stream));
+}
+
+int alv_ffn(alv_ctx* ctx, alv_handle h, int ntok, const void* x, int x_dtype, void* y, int y_dtype,
+            void* stream) {
+  if (!ctx || !x || !y || !valid_dtype(x_dtype) || !valid_dtype(y_dtype))
+    return fail(ctx, ALV_ERR_ARG, "ffn: bad argument");
+  Weight* w = get_weight(ctx, h, 2);
+  if (!w) return fail(ctx, ALV_ERR_HANDLE, "ffn: invalid handle (not an ffn weight)");
+  int rc = set_device(ctx);
+  if (rc) return rc;
+  FfnIo io;
+  io.x = x;
+  io.x_dtype = x_dtype;
+  io.y32 = y_dtype == ALV_F32 ? static_cast<float*>(y) : nullptr;
+  io.y16 = y_dtype == ALV_BF16 ? static_cast<uint16_t*>(y) : nullptr;
+  return do_ffn(ctx, w, ntok, io, static_cast<cudaStream_t>(stream));
+}
+
+int alv_ffn_layer(alv_ctx* ctx, alv_handle h, int ntok, const uint16_t* x_in, const float* down_in,
+                  uint16_t* x_out, float* down_out, void* stream) {
+  if (!ctx || !x_in || !down_out) return fail(ctx, ALV_ERR_ARG, "ffn_layer: bad argument");
+  Weight* w = get_weight(ctx, h, 2);
+  if (!w) return fail(ctx, ALV_ERR_HANDLE, "ffn_layer: invalid handle (not an ffn weight)");
+  int rc = set_device(ctx);
+  if (rc) return rc;
+  FfnIo io;
+  io.x = x_in;
+  io.x_dtype = ALV_BF16;
+  io.glue = 1;
+  io.x_in = x_in;
+  io.down_in = down_in;
+  io.x_out = x_out;
+  io.y32 = down_out;
+  return do_ffn(ctx, w, ntok, io, static_cast<cudaStream_t>(stream));
+}
+
+int alv_ffn_stack_finalize(alv_ctx* ctx, int ntok, int H, const uint16_t* x_in, const float* down_in,
+                           uint16_t* x_out, void* stream) {
+  if (!ctx || !x_in || !down_in || !x_out || ntok < 1 || H <= 0)
+    return fail(ctx, ALV_ERR_ARG, "ffn_stack_finalize: bad argument");
+  int rc = set_device(ctx);
+  if (rc) return rc;
+  ffn_stack_finalize_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(
+      ntok, static_cast<uint32_t>(H), x_in, down_in, x_out, 1e-6f);
+  ALV_CUDA(ctx, cudaGetLastError());
+  return ALV_OK;
+}
+
+static int run_host(alv_ctx* ctx, alv_handle h, int kind, int ntok, const void* x_host, int x_dtype,
+                    void* y_host, int y_dtype) {
+  if (!ctx || !x_host || !y_host || !valid_dtype(x_dtype) || !valid_dtype(y_dtype) || ntok < 1)
+    return fail(ctx, ALV_ERR_ARG, "run: bad argument");
+  Weight* w = get_weight(ctx, h, kind);
+  if (!w) return fail(ctx, ALV_ERR_HANDLE, "run: invalid handle");
+  int rc = set_device(ctx);
+  if (rc) return rc;
+  const size_t K = kind == 1 ? w->a.cols : w->H;
+  const size_t N = kind == 1 ? w->a.rows : w->H;
+  const size_t xb = static_cast<size_t>(ntok) * K * (x_dtype == ALV_F32 ? 4 : 2);
+  const size_t yb = static_cast<size_t>(ntok) * N * (y_dtype == ALV_F32 ? 4 : 2);
+  rc = io_buffers(ctx, align_up(xb, 256) + yb);
+  if (rc) return rc;
+  uint8_t* dx = static_cast<uint8_t*>(ctx->io);
+  uint8_t* dy = dx + align_up(xb, 256);
+  ALV_CUDA(ctx, cudaMemcpyAsync(dx, x_host, xb, cudaMemcpyHostToDevice, ctx->stream));
+  if (kind == 1) {
+    rc = do_gemv(ctx, w, ntok, dx, x_dtype, dy, y_dtype, ctx->stream);
+  } else {
+    FfnIo io;
+    io.x = dx;
+    io.x_dtype = x_dtype;
+    io.y32 = y_dtype == ALV_F32 ? reinterpret_cast<float*>(dy) : nullptr;
+    io.y16 = y_dtype == ALV_BF16 ? reinterpret_cast<uint16_t*>(dy) : nullptr;
+    rc = do_ffn(ctx, w, ntok, io, ctx->stream);
+  }
+  if (rc) return rc;
+  ALV_CUDA(ctx, cudaMemcpyAsync(y_host, dy, yb, cudaMemcpyDeviceToHost, ctx->stream));
+  return check_status(ctx, ctx->stream);
+}
+
+int alv_run_gemv(alv_ctx* ctx, alv_handle h, int ntok, const void* x_host, int x_dtype, void* y_host,
+                 int y_dtype) {
+  return run_host(ctx, h, 1, ntok, x_host, x_dtype, y_host, y_dtype);
+}
+
+int alv_run_ffn(alv_ctx* ctx, alv_handle h, int ntok, const void* x_host, int x_dtype, void* y_host,
+                int y_dtype) {
+  return run_host(ctx, h, 2, ntok, x_host, x_dtype, y_host, y_dtype);
+}
+
+}  // extern "C"

@@ -1,0 +1,571 @@
+// Device kernels of the Q4 decode hot path: GPU quantizer, load-time repack,
+// dequantize, gemv (decode / decode-batch), the fused FFN and the FFN-stack
+// layer glue.  Host launchers live in alveare.cu.
+#pragma once
+
+#include <climits>
+
+#include "common.cuh"
+#include "stream.cuh"
+
+namespace alv {
+
+constexpr int kWarpsPerCta = 16;
+
+// ===========================================================================
+// GPU quantizer: restates tools/convert/gemv_q_convert.py:5-85.
+// One thread per (row, 32-block); writes one 20-byte reference block.
+// ===========================================================================
+__global__ void q4_quantize_kernel(const float* __restrict__ W, int N, int K,
+                                   uint8_t* __restrict__ out) {
+  const int KB = K / 32;
+  const size_t t = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (t >= static_cast<size_t>(N) * KB) return;
+  const size_t row = t / KB, b = t % KB;
+  const float* w = W + row * K + b * 32;
+  float v[32];
+  float mx = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    v[i] = w[i];
+    mx = fmaxf(mx, fabsf(v[i]));
+  }
+  float s = __fdiv_rn(mx, 7.0f);       // max_vals / 7.0 in float32 (:24-25)
+  if (s == 0.0f) s = 1.0f;             // (:27-28)
+  // The 20-byte block is 4-byte aligned: write it as five 32-bit words.
+  uint32_t* dst = reinterpret_cast<uint32_t*>(out + row * (static_cast<size_t>(KB) * 20) + b * 20);
+#pragma unroll
+  for (int wd = 0; wd < 4; ++wd) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = wd * 4 + j;
+      int q0 = static_cast<int>(rintf(__fdiv_rn(v[2 * i], s)));      // half-to-even (:34)
+      int q1 = static_cast<int>(rintf(__fdiv_rn(v[2 * i + 1], s)));
+      q0 = min(max(q0, -8), 7);                                    // (:37)
+      q1 = min(max(q1, -8), 7);
+      word |= static_cast<uint32_t>((q0 & 0x0F) | ((q1 & 0x0F) << 4)) << (8 * j);  // (:45-48)
+    }
+    dst[wd] = word;
+  }
+  // scales.astype(bfloat16) (:51): round-to-nearest-even of a finite float.
+  const uint32_t su = __float_as_uint(s);
+  dst[4] = (su + 0x7FFFu + ((su >> 16) & 1u)) >> 16;  // bytes 16-17 scale, 18-19 zero
+}
+
+// ===========================================================================
+// Load-time repack: reference (N, K/32*20) blocks -> unit layout (stream.cuh).
+// ===========================================================================
+struct RepackSrc {
+  const uint8_t* a;      // primary source rows (gemv matrix, FFN gate, FFN down)
+  const uint8_t* b;      // FFN up (interleave8) or null
+  uint32_t rows;         // valid source rows in the selected slice
+  uint32_t row_off;      // first source row (TP slice of gate/up)
+  uint64_t row_bytes;    // source row stride in bytes
+  uint32_t blk_off;      // first source 32-block (TP slice of down)
+  uint32_t K;            // valid columns (multiple of 32)
+  uint32_t interleave8;  // tile rows 0-7 from a, 8-15 from b (same source rows)
+  uint32_t RT, KT;       // destination tiles
+
+  // Pointer to block 0 of destination row R, or null for padding rows.
+  __device__ __forceinline__ const uint8_t* row_ptr(uint32_t R) const {
+    uint32_t sr;
+    const uint8_t* buf;
+    if (interleave8) {
+      const uint32_t rr = R & 15;
+      sr = (R >> 4) * 8 + (rr & 7);
+      buf = rr < 8 ? a : b;
+    } else {
+      sr = R;
+      buf = a;
+    }
+    if (sr >= rows) return nullptr;
+    return buf + (static_cast<uint64_t>(row_off) + sr) * row_bytes + static_cast<uint64_t>(blk_off) * 20;
+  }
+};
+
+__device__ __forceinline__ bool block_all_zero(const uint8_t* blk) {
+  uint32_t acc = 0;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) acc |= blk[i];
+  return acc == 0;
+}
+
+__device__ __forceinline__ float block_scale(const uint8_t* blk) {
+  return bf16_bits_to_f32(static_cast<uint32_t>(blk[16]) | (static_cast<uint32_t>(blk[17]) << 8));
+}
+
+// Scale-exponent survey over the blocks that carry a nonzero q: ilogb range
+// and a non-finite flag.  info = {emax, emin, nonfinite}.
+__global__ void q4_scale_survey_kernel(RepackSrc s, int* info) {
+  const uint32_t KB = s.K / 32;
+  const uint64_t t = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (t >= static_cast<uint64_t>(s.RT) * 16 * KB) return;
+  const uint32_t R = static_cast<uint32_t>(t / KB), B = static_cast<uint32_t>(t % KB);
+  const uint8_t* p = s.row_ptr(R);
+  if (!p) return;
+  const uint8_t* blk = p + static_cast<uint64_t>(B) * 20;
+  if (block_all_zero(blk)) return;
+  const float sc = block_scale(blk);
+  if (sc == 0.f) return;
+  if (!isfinite(sc)) {
+    atomicOr(&info[2], 1);
+    return;
+  }
+  const int e = ilogbf(sc);
+  atomicMax(&info[0], e);
+  atomicMin(&info[1], e);
+}
+
+// One thread per destination 32-bit word (144 per unit).
+__global__ void q4_repack_kernel(RepackSrc s, int fast, int je, uint32_t* __restrict__ out) {
+  const uint64_t t = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const uint64_t nunits = static_cast<uint64_t>(s.RT) * s.KT;
+  if (t >= nunits * 144) return;
+  const uint64_t unit = t / 144;
+  const uint32_t wi = static_cast<uint32_t>(t % 144);
+  const uint32_t r = static_cast<uint32_t>(unit / s.KT), kt = static_cast<uint32_t>(unit % s.KT);
+  uint32_t word = 0;
+  if (wi < 128) {
+    const uint32_t L = wi >> 2, j = wi & 3, g = L >> 2, t4 = L & 3;
+    const uint32_t c = kt * 64 + j * 16 + 2 * t4;
+    uint32_t u[2][4];  // [row g / g+8][col c, c+1, c+8, c+9]
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint8_t* p = s.row_ptr(r * 16 + g + 8 * h);
+      if (p && c < s.K) {
+        const uint8_t* blk = p + static_cast<uint64_t>(c / 32) * 20;
+        const uint8_t b0 = blk[(c % 32) / 2], b8 = blk[(c % 32) / 2 + 4];
+        u[h][0] = (b0 & 15u) ^ 8u;
+        u[h][1] = (b0 >> 4) ^ 8u;
+        u[h][2] = (b8 & 15u) ^ 8u;
+        u[h][3] = (b8 >> 4) ^ 8u;
+      } else {
+        u[h][0] = u[h][1] = u[h][2] = u[h][3] = 8u;
+      }
+    }
+    word = u[0][0] | (u[1][0] << 4) | (u[0][2] << 8) | (u[1][2] << 12) | (u[0][1] << 16) |
+           (u[1][1] << 20) | (u[0][3] << 24) | (u[1][3] << 28);
+  } else {
+    const uint32_t sw = wi - 128, g = sw >> 1, h = sw & 1;
+    const uint8_t* p = s.row_ptr(r * 16 + g + 8 * h);
+    uint32_t half[2];
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+      const uint32_t B = kt * 2 + b;
+      half[b] = 0;
+      if (p && B * 32 < s.K) {
+        const uint8_t* blk = p + static_cast<uint64_t>(B) * 20;
+        const uint32_t bits = static_cast<uint32_t>(blk[16]) | (static_cast<uint32_t>(blk[17]) << 8);
+        if (!fast) {
+          half[b] = bits;  // generic path: the scale as stored (exact numpy semantics)
+        } else if (!block_all_zero(blk) && bf16_bits_to_f32(bits) != 0.f) {
+          // s * 2^(133 - je): exact exponent shift of a bf16 value.
+          half[b] = __float_as_uint(ldexpf(bf16_bits_to_f32(bits), 133 - je)) >> 16;
+        }
+      }
+    }
+    word = half[0] | (half[1] << 16);
+  }
+  out[t] = word;
+}
+
+// Dequantize a unit-layout matrix to bf16 (rows x K row-major).
+__global__ void q4_dequant_kernel(Q4Mat m, uint32_t rows, uint32_t K, uint16_t* __restrict__ out) {
+  const uint64_t t = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const uint64_t nunits = static_cast<uint64_t>(m.RT) * m.KT;
+  if (t >= nunits * 32) return;
+  const uint64_t unit = t >> 5;
+  const int lane = static_cast<int>(t & 31), g = lane >> 2, t4 = lane & 3;
+  const uint32_t r = static_cast<uint32_t>(unit / m.KT), kt = static_cast<uint32_t>(unit % m.KT);
+  const uint8_t* ub = m.units + unit * kUnitBytes;
+  const uint4 nib = *reinterpret_cast<const uint4*>(ub + lane * 16);
+  const uint2 sc = *reinterpret_cast<const uint2*>(ub + kUnitNibBytes + g * 8);
+  const bool fast = m.fast != 0;
+  uint32_t S[2][2], C[2][2];
+  S[0][0] = (sc.x & 0xFFFF) * 0x10001u;
+  S[1][0] = (sc.x >> 16) * 0x10001u;
+  S[0][1] = (sc.y & 0xFFFF) * 0x10001u;
+  S[1][1] = (sc.y >> 16) * 0x10001u;
+  for (int b = 0; b < 2; ++b)
+    for (int h = 0; h < 2; ++h) C[b][h] = fast ? bf2_mul(S[b][h], kNeg8Sub) : 0u;
+  const uint32_t words[4] = {nib.x, nib.y, nib.z, nib.w};
+  for (int j = 0; j < 4; ++j) {
+    const int b = j >> 1;
+    uint32_t a[4];
+    if (fast)
+      dequant_word<true>(words[j], S[b][0], C[b][0], S[b][1], C[b][1], a);
+    else
+      dequant_word<false>(words[j], S[b][0], C[b][0], S[b][1], C[b][1], a);
+    const uint32_t c = kt * 64 + j * 16 + 2 * t4;
+    const uint32_t rowv[4] = {r * 16 + g, r * 16 + g + 8, r * 16 + g, r * 16 + g + 8};
+    const uint32_t colv[4] = {c, c, c + 8, c + 8};
+    for (int i = 0; i < 4; ++i) {
+      if (rowv[i] >= rows || colv[i] >= K) continue;
+      for (int e = 0; e < 2; ++e) {
+        const uint32_t bits = e ? (a[i] >> 16) : (a[i] & 0xFFFF);
+        const float v = bf16_bits_to_f32(bits) * m.scale_mul;  // exact power-of-two scaling
+        out[static_cast<uint64_t>(rowv[i]) * K + colv[i] + e] = bf16_bits_rn(v);
+      }
+    }
+  }
+}
+
+// ===========================================================================
+// Activation sources / epilogues
+// ===========================================================================
+struct XSrc {  // (ntok, K) activations, fp32 or bf16, row stride ld
+  const void* x;
+  int bf16;
+  int ntok;
+  uint32_t K;
+  uint32_t ld;
+  // Values at (tok, k) and (tok, k+1), k even; zero outside [0, ntok) x [0, K).
+  // K is a multiple of 32, so k < K implies k + 1 < K.
+  __device__ __forceinline__ void pair(uint32_t tok, uint32_t k, float& a, float& b) const {
+    if (static_cast<int>(tok) >= ntok || k >= K) {
+      a = b = 0.f;
+      return;
+    }
+    const uint64_t i = static_cast<uint64_t>(tok) * ld + k;
+    if (bf16) {
+      const uint32_t w = __ldg(reinterpret_cast<const unsigned int*>(static_cast<const uint16_t*>(x) + i));
+      a = bf16_bits_to_f32(w & 0xFFFF);
+      b = bf16_bits_to_f32(w >> 16);
+    } else {
+      const float2 f = __ldg(reinterpret_cast<const float2*>(static_cast<const float*>(x) + i));
+      a = f.x;
+      b = f.y;
+    }
+  }
+};
+
+struct SmemSrc {  // staged activations in shared memory: float[ntok][K]
+  const float* v;
+  int ntok;
+  uint32_t K;
+  __device__ __forceinline__ void pair(uint32_t tok, uint32_t k, float& a, float& b) const {
+    if (static_cast<int>(tok) >= ntok || k >= K) {
+      a = b = 0.f;
+      return;
+    }
+    a = v[static_cast<uint64_t>(tok) * K + k];
+    b = v[static_cast<uint64_t>(tok) * K + k + 1];
+  }
+};
+
+struct ActSrc {  // FFN intermediate written by other CTAs: read through L2
+  const uint16_t* act;
+  int ntok;
+  uint32_t I;
+  uint32_t ld;
+  __device__ __forceinline__ void pair(uint32_t tok, uint32_t k, float& a, float& b) const {
+    if (static_cast<int>(tok) >= ntok || k >= I) {
+      a = b = 0.f;
+      return;
+    }
+    const uint32_t w = __ldcg(reinterpret_cast<const unsigned int*>(act + static_cast<uint64_t>(tok) * ld + k));
+    a = bf16_bits_to_f32(w & 0xFFFF);
+    b = bf16_bits_to_f32(w >> 16);
+  }
+};
+
+struct RowsEpi {  // y[tok, row] = v * scale_mul (fp32 and/or bf16)
+  float* y32;
+  uint16_t* y16;
+  uint32_t N;
+  uint32_t ld;
+  float sm;
+  __device__ __forceinline__ void put(int tok, uint32_t row, float v) const {
+    if (row >= N) return;
+    const uint64_t i = static_cast<uint64_t>(tok) * ld + row;
+    v *= sm;
+    if (y32) y32[i] = v;
+    if (y16) y16[i] = bf16_bits_rn(v);
+  }
+  __device__ __forceinline__ void apply(uint32_t r, int g, int tok, float vg, float vg8) const {
+    put(tok, r * 16 + g, vg);
+    put(tok, r * 16 + g + 8, vg8);
+  }
+};
+
+// GeGLU exactly as runtime/py/model.py:690-693 evaluates it under numpy
+// promotion: float32 cubic term, float64 from the sqrt(2/pi) factor on,
+// float64 -> float32 before the bf16 cast.
+__device__ __forceinline__ float geglu_ref(float g, float u) {
+  const float g3 = __fmul_rn(__fmul_rn(g, g), g);                 // exact for bf16 g
+  const float inner = __fadd_rn(g, __fmul_rn(0x1.6e4e26p-5f, g3));  // g + 0.044715f * g^3
+  const double t = tanh(0x1.9884533d43651p-1 * static_cast<double>(inner));  // np.sqrt(2/np.pi)
+  const double gelu = static_cast<double>(__fmul_rn(0.5f, g)) * (1.0 + t);
+  return static_cast<float>(gelu * static_cast<double>(u));
+}
+
+// SwiGLU as runtime/py/model.py:857-859 (float32 throughout).
+__device__ __forceinline__ float swiglu_ref(float g, float u) {
+  const float e = static_cast<float>(exp(-static_cast<double>(g)));  // correctly rounded expf
+  const float s = __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
+  return __fmul_rn(__fmul_rn(g, s), u);
+}
+
+struct GateUpEpi {  // tile rows 0-7 gate, 8-15 up of the same 8 intermediate indices
+  uint16_t* act;
+  uint32_t I;
+  uint32_t ld;
+  float sm;
+  int fn;
+  __device__ __forceinline__ void apply(uint32_t r, int g, int tok, float vg, float vg8) const {
+    const uint32_t i = r * 8 + g;
+    if (i >= I) return;
+    const float gate = bf16_round(vg * sm), up = bf16_round(vg8 * sm);
+    const float a = fn == 0 ? geglu_ref(gate, up) : swiglu_ref(gate, up);
+    act[static_cast<uint64_t>(tok) * ld + i] = bf16_bits_rn(a);
+  }
+};
+
+// ===========================================================================
+// Grid-wide barrier (sense by generation counter), bounded wait.
+// ===========================================================================
+struct GridBar {
+  uint32_t count;
+  uint32_t gen;
+};
+
+__device__ bool grid_barrier(GridBar* gb, uint32_t nblocks, uint32_t* status) {
+  __syncthreads();
+  int ok = 1;
+  if (threadIdx.x == 0) {
+    volatile uint32_t* vgen = &gb->gen;
+    const uint32_t gen = *vgen;
+    __threadfence();
+    const uint32_t arrived = atomicAdd(&gb->count, 1u);
+    if (arrived == nblocks - 1) {
+      atomicExch(&gb->count, 0u);
+      __threadfence();
+      atomicAdd(&gb->gen, 1u);
+    } else {
+      const unsigned long long t0 = globaltimer_ns();
+      while (*vgen == gen) {
+        __nanosleep(64);
+        if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+          atomicOr(status, kStatusGridTimeout);
+          ok = 0;
+          break;
+        }
+      }
+    }
+    __threadfence();
+  }
+  return __syncthreads_and(ok) != 0;
+}
+
+// Block-wide sum (all threads get the result); red holds >= 32 floats.
+__device__ float block_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float s = 0.f;
+  for (int i = 0; i < nw; ++i) s += red[i];  // fixed order: identical in every CTA
+  __syncthreads();
+  return s;
+}
+
+// ===========================================================================
+// gemv: persistent, one CTA per SM, stream-K over units.
+// ===========================================================================
+struct GemvParams {
+  Q4Mat m;
+  XSrc x;
+  RowsEpi epi;
+  Fixup fx;
+  uint32_t* status;
+  uint32_t nst;  // ring stages per warp
+};
+
+constexpr int kUnitsPerStage = 4;
+
+template <int UPS>
+__device__ __forceinline__ void ring_place(WarpRing<UPS>& ring, uint8_t* smem, int warp, uint32_t nst) {
+  constexpr size_t stage_bytes = WarpRing<UPS>::kStageBytes;
+  ring.nst = nst;
+  ring.ring = smem + static_cast<size_t>(warp) * nst * stage_bytes;
+  ring.bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(kWarpsPerCta) * nst * stage_bytes) +
+              warp * nst;
+  ring.policy = l2_policy_evict_first();
+}
+
+__host__ __device__ constexpr size_t ring_smem_bytes(uint32_t nst) {
+  return static_cast<size_t>(kWarpsPerCta) * nst * (kUnitsPerStage * kUnitBytes + 8);
+}
+
+template <int NCOLS, bool SPLIT, bool FAST>
+__global__ void __launch_bounds__(kWarpsPerCta * 32, 1) gemv_kernel(const GemvParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t gw = participant_index(blockIdx.x, warp, gridDim.x);
+  const uint64_t U = static_cast<uint64_t>(p.m.RT) * p.m.KT;
+  const uint64_t W = effective_warps(static_cast<uint64_t>(gridDim.x) * kWarpsPerCta, U, p.m.KT);
+  uint32_t u0 = 0, u1 = 0;
+  if (gw < W) {
+    u0 = static_cast<uint32_t>(range_start(gw, U, W));
+    u1 = static_cast<uint32_t>(range_start(gw + 1, U, W));
+  }
+  WarpRing<kUnitsPerStage> ring;
+  ring_place(ring, smem, warp, p.nst);
+  ring.setup(p.m.units + static_cast<size_t>(u0) * kUnitBytes, u1 - u0, p.m.units, 0);
+  ring.init_and_prime(lane);
+
+  uint8_t* xs = smem + ring_smem_bytes(p.nst);
+  stage_frags<NCOLS, SPLIT>(xs, p.m.KT, p.x);
+  __syncthreads();
+  consume_range<NCOLS, SPLIT, FAST>(ring, p.m, u0, u1, xs, p.fx, gw, static_cast<uint32_t>(W), p.x.ntok,
+                                    p.epi, p.status);
+}
+
+// ===========================================================================
+// Fused FFN: phase A (gate/up interleaved, activation epilogue -> act),
+// grid barrier, phase B (down projection).  The per-warp ring prefetches
+// phase-B weights while phase A finishes and the barrier is pending.
+// ===========================================================================
+struct FfnParams {
+  Q4Mat gu;
+  Q4Mat dn;
+  uint32_t H;
+  uint32_t I;
+  int fn;
+  int ntok;
+  XSrc x;               // plain input (glue == 0)
+  int glue;             // 1: x is the bf16 residual stream, norms/residual fused
+  const uint16_t* x_in;
+  const float* down_in;
+  uint16_t* x_out;
+  float eps;
+  RowsEpi out;          // down projection output
+  uint16_t* act;        // scratch [ntok][act_ld]
+  uint32_t act_ld;
+  Fixup fxA, fxB;
+  GridBar* bar;
+  uint32_t* status;
+  uint32_t nst;  // ring stages per warp
+};
+
+// Glue prologue: build x = bf16(x_in + bf16(rmsnorm(bf16(down_in)))) and
+// xn = bf16(rmsnorm(x)) per token into tmp[ntok][H] (fp32 holding bf16 values).
+__device__ void ffn_glue_prologue(const FfnParams& p, float* tmp, float* red) {
+  const uint32_t H = p.H;
+  const float hf = static_cast<float>(H);  // np.mean divides the float32 sum by n
+  for (int tok = 0; tok < p.ntok; ++tok) {
+    float* xt = tmp + static_cast<size_t>(tok) * H;
+    const uint16_t* xi = p.x_in + static_cast<size_t>(tok) * H;
+    if (p.down_in) {
+      const float* di = p.down_in + static_cast<size_t>(tok) * H;
+      float ss = 0.f;
+      for (uint32_t h = threadIdx.x; h < H; h += blockDim.x) {
+        const float d = bf16_round(di[h]);
+        xt[h] = d;
+        ss = fmaf(d, d, ss);
+      }
+      ss = block_sum(ss, red);
+      const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, hf), p.eps)));
+      for (uint32_t h = threadIdx.x; h < H; h += blockDim.x) {
+        const float dn = bf16_round(xt[h] * inv);
+        xt[h] = bf16_round(bf16_bits_to_f32(xi[h]) + dn);
+      }
+    } else {
+      for (uint32_t h = threadIdx.x; h < H; h += blockDim.x) xt[h] = bf16_bits_to_f32(xi[h]);
+    }
+    __syncthreads();
+    if (blockIdx.x == 0 && p.x_out) {
+      for (uint32_t h = threadIdx.x; h < H; h += blockDim.x)
+        p.x_out[static_cast<size_t>(tok) * H + h] = bf16_bits_rn(xt[h]);
+    }
+    float ss = 0.f;
+    for (uint32_t h = threadIdx.x; h < H; h += blockDim.x) ss = fmaf(xt[h], xt[h], ss);
+    ss = block_sum(ss, red);
+    const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, hf), p.eps)));
+    for (uint32_t h = threadIdx.x; h < H; h += blockDim.x) xt[h] = bf16_round(xt[h] * inv);
+    __syncthreads();
+  }
+}
+
+template <int NT, bool SPLIT, bool FAST>
+__global__ void __launch_bounds__(kWarpsPerCta * 32, 1) ffn_kernel(const FfnParams p) {
+  constexpr int NCA = SPLIT ? 2 * NT : NT;
+  constexpr int NCB = NT;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t gw = participant_index(blockIdx.x, warp, gridDim.x);
+  const uint64_t Wtot = static_cast<uint64_t>(gridDim.x) * kWarpsPerCta;
+  const uint64_t UA = static_cast<uint64_t>(p.gu.RT) * p.gu.KT;
+  const uint64_t UB = static_cast<uint64_t>(p.dn.RT) * p.dn.KT;
+  const uint64_t WA = effective_warps(Wtot, UA, p.gu.KT), WB = effective_warps(Wtot, UB, p.dn.KT);
+  uint32_t a0 = 0, a1 = 0, b0 = 0, b1 = 0;
+  if (gw < WA) {
+    a0 = static_cast<uint32_t>(range_start(gw, UA, WA));
+    a1 = static_cast<uint32_t>(range_start(gw + 1, UA, WA));
+  }
+  if (gw < WB) {
+    b0 = static_cast<uint32_t>(range_start(gw, UB, WB));
+    b1 = static_cast<uint32_t>(range_start(gw + 1, UB, WB));
+  }
+  WarpRing<kUnitsPerStage> ring;
+  ring_place(ring, smem, warp, p.nst);
+  ring.setup(p.gu.units + static_cast<size_t>(a0) * kUnitBytes, a1 - a0,
+             p.dn.units + static_cast<size_t>(b0) * kUnitBytes, b1 - b0);
+  ring.init_and_prime(lane);
+
+  uint8_t* xs = smem + ring_smem_bytes(p.nst);
+  const size_t xs_bytes_a = frag_bytes(p.gu.KT, NCA);
+  const size_t xs_bytes_b = frag_bytes(p.dn.KT, NCB);
+  const size_t xs_bytes = xs_bytes_a > xs_bytes_b ? xs_bytes_a : xs_bytes_b;
+  float* red = reinterpret_cast<float*>(xs + xs_bytes);
+  float* tmp = red + 32;
+
+  if (p.glue) {
+    ffn_glue_prologue(p, tmp, red);
+    stage_frags<NCA, false>(xs, p.gu.KT, SmemSrc{tmp, p.ntok, p.H});
+  } else {
+    stage_frags<NCA, SPLIT>(xs, p.gu.KT, p.x);
+  }
+  __syncthreads();
+
+  GateUpEpi ge{p.act, p.I, p.act_ld, p.gu.scale_mul, p.fn};
+  const bool ok = consume_range<NCA, SPLIT, FAST>(ring, p.gu, a0, a1, xs, p.fxA, gw, static_cast<uint32_t>(WA),
+                                                  p.ntok, ge, p.status);
+  const bool bar_ok = grid_barrier(p.bar, gridDim.x, p.status);
+  if (!bar_ok || !__syncthreads_and(ok)) {
+    if (ok) ring.drain();
+    return;
+  }
+  stage_frags<NCB, false>(xs, p.dn.KT, ActSrc{p.act, p.ntok, p.I, p.act_ld});
+  __syncthreads();
+  consume_range<NCB, false, FAST>(ring, p.dn, b0, b1, xs, p.fxB, gw, static_cast<uint32_t>(WB), p.ntok, p.out,
+                                  p.status);
+}
+
+// Final residual of an FFN stack (single CTA).
+__global__ void ffn_stack_finalize_kernel(int ntok, uint32_t H, const uint16_t* x_in,
+                                          const float* down_in, uint16_t* x_out, float eps) {
+  __shared__ float red[32];
+  const float hf = static_cast<float>(H);
+  for (int tok = 0; tok < ntok; ++tok) {
+    const float* di = down_in + static_cast<size_t>(tok) * H;
+    const uint16_t* xi = x_in + static_cast<size_t>(tok) * H;
+    float ss = 0.f;
+    for (uint32_t h = threadIdx.x; h < H; h += blockDim.x) {
+      const float d = bf16_round(di[h]);
+      ss = fmaf(d, d, ss);
+    }
+    ss = block_sum(ss, red);
+    const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, hf), eps)));
+    for (uint32_t h = threadIdx.x; h < H; h += blockDim.x) {
+      const float dn = bf16_round(bf16_round(di[h]) * inv);
+      x_out[static_cast<size_t>(tok) * H + h] = bf16_bits_rn(bf16_bits_to_f32(xi[h]) + dn);
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace alv

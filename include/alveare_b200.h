@@ -1,0 +1,160 @@
+/*
+ * alveare_b200 -- C ABI of the B200 (sm_100a) Q4 decode hot path.
+ *
+ * Drop-in replacement for the NPU boundary of daino-selvatico/alveare:
+ *   C++ registry   runtime/cpp/include/alveare/npu.h:44-115 (NpuRegistry)
+ *   Python ops     kernels/gemv_q/gemv_q.py:33-43   gemv_q_npu
+ *                  kernels/ffn_fused/ffn_fused.py:28-39 ffn_fused_npu
+ *                  kernels/gemm_q/gemm_q.py:28-39   gemm_q_npu
+ *
+ * Conventions
+ *  - Plain pointers and sizes only.  `stream` is a cudaStream_t passed as
+ *    void* (NULL = legacy default stream).  Device pointers unless a
+ *    function says "host".
+ *  - Every function returns an alv_status (0 = ok).  No exceptions cross the
+ *    ABI; alv_last_error() gives a message for the last failure on a context
+ *    (the reference throws std::runtime_error instead, npu.cpp:272-276).
+ *  - Weights are given in the reference's packed Q4 layout: (N, K/32*20)
+ *    uint8, each 20-byte block = 16 B nibbles (even k low nibble) + bf16
+ *    scale (LE) + 2 B pad (tools/convert/gemv_q_convert.py:53-85).  They are
+ *    repacked once on the GPU into the library's own layout and referenced
+ *    by an opaque handle afterwards (npu.h:28-30, 64-72).
+ *  - Activation dtypes: ALV_F32 or ALV_BF16.  fp32 inputs are consumed at
+ *    full fp32 precision; outputs are fp32 or bf16 (round-to-nearest-even).
+ *  - A context belongs to one device and is thread-compatible, not
+ *    thread-safe: calls on one context must be serialized and use one stream
+ *    at a time (the reference serializes requests with a mutex,
+ *    generator.h:39-42).  Kernel launches are stream-ordered and
+ *    asynchronous; alv_sync_status() synchronizes and reports device-side
+ *    failures (a bounded wait that timed out).
+ */
+#ifndef ALVEARE_B200_H
+#define ALVEARE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct alv_ctx alv_ctx;
+typedef uint32_t alv_handle; /* 0 is never a valid handle */
+
+typedef enum {
+  ALV_OK = 0,
+  ALV_ERR_ARG = 1,          /* bad pointer, size or enum */
+  ALV_ERR_HANDLE = 2,       /* unknown or wrong-kind weight handle */
+  ALV_ERR_SHAPE = 3,        /* shape mismatch / unsupported divisibility */
+  ALV_ERR_CUDA = 4,         /* CUDA runtime error (message in alv_last_error) */
+  ALV_ERR_TIMEOUT = 5,      /* a device-side bounded wait gave up */
+  ALV_ERR_UNSUPPORTED = 6,  /* valid request outside this build's limits */
+  ALV_ERR_NO_DEVICE = 7     /* no usable sm_100 device */
+} alv_status;
+
+enum { ALV_F32 = 0, ALV_BF16 = 1 };
+enum { ALV_ACT_GELU = 0, ALV_ACT_SILU = 1 };
+
+/* Library version (major*10000 + minor*100 + patch). */
+int alv_version(void);
+
+/* Create / destroy a context on CUDA device `device`.  Replaces the
+ * NpuRegistry constructor/destructor (npu.h:48-51). */
+int alv_ctx_create(int device, alv_ctx** out);
+int alv_ctx_destroy(alv_ctx* ctx);
+const char* alv_last_error(const alv_ctx* ctx);
+
+/* Synchronize `stream` and report any device-side failure recorded since the
+ * last call (ALV_ERR_TIMEOUT).  Clears the recorded status. */
+int alv_sync_status(alv_ctx* ctx, void* stream);
+
+/* ---- Q4 format on the GPU ------------------------------------------------ */
+
+/* Quantize a float32 (N, K) row-major device matrix into the reference's
+ * packed layout (N, K/32*20) on the device.  GPU restatement of
+ * quantize_to_q4_0 + pack_to_combined (tools/convert/gemv_q_convert.py:5-85):
+ * per 32-block scale = max|w|/7 (0 -> 1.0), q = clip(rint(w/scale), -8, 7),
+ * scale stored as bf16.  K must be a multiple of 32. */
+int alv_q4_quantize(alv_ctx* ctx, const float* w, int N, int K, uint8_t* combined, void* stream);
+
+/* ---- weights (NpuRegistry::create_*_weight, npu.h:64-72) ------------------ */
+
+/* Register an (N, K) Q4 matrix for gemv/gemm.  `combined` holds N*(K/32)*20
+ * bytes in the reference layout, on the host (on_device = 0) or the device
+ * (on_device = 1).  Replaces NpuRegistry::create_gemv_weight (npu.h:68-69). */
+int alv_gemv_weight_create(alv_ctx* ctx, int N, int K, const void* combined, size_t nbytes,
+                           int on_device, alv_handle* out);
+
+/* Register a fused FFN from its three per-matrix packed buffers:
+ * gate, up: (I, H/32*20); down: (H, I/32*20).  [i_begin, i_end) selects the
+ * slice of the intermediate dimension this device holds (tensor-parallel
+ * split, multiples of 32; pass 0, I for the whole FFN).  act = ALV_ACT_*.
+ * Replaces NpuRegistry::create_ffn_fused_weight (npu.h:71-72) together with
+ * the load-time repack pack_ffn_fused_weights (runtime/cpp/src/weights.cpp:94-190). */
+int alv_ffn_weight_create(alv_ctx* ctx, int H, int I, int act, const void* gate, const void* up,
+                          const void* down, int on_device, int i_begin, int i_end,
+                          alv_handle* out);
+
+int alv_weight_destroy(alv_ctx* ctx, alv_handle h);
+
+/* Change the activation of a registered FFN (the reference passes it per
+ * call: NpuRegistry::run_ffn_fused, npu.h:94-95; ffn_fused_npu(activation=)). */
+int alv_ffn_set_activation(alv_ctx* ctx, alv_handle h, int act);
+
+/* info[0..7] = kind (1 gemv, 2 ffn), rows (N or H), cols (K or local I),
+ * fast-dequant flag of matrix 0, of matrix 1, device bytes, i_begin, i_end. */
+int alv_weight_info(alv_ctx* ctx, alv_handle h, int64_t* info);
+
+/* Dequantize a registered matrix back to bf16 (rows x cols row-major) on the
+ * device, with the same arithmetic the kernels use.  which: 0 = gemv matrix
+ * or FFN gate, 1 = FFN up, 2 = FFN down.  GPU counterpart of
+ * dequantize_combined (tools/ref/gemv_q.py:39-62). */
+int alv_weight_dequantize(alv_ctx* ctx, alv_handle h, int which, uint16_t* out, void* stream);
+
+/* ---- compute (device pointers, stream-ordered) ---------------------------- */
+
+/* y[t, n] = sum_k W[n, k] * x[t, k] for t < ntok (1 <= ntok <= 16; fp32 x
+ * allows ntok <= 8).  x is (ntok, K), y is (ntok, N), both row-major.
+ * Replaces NpuRegistry::run_gemv / run_gemm (npu.cpp:269-312) and the
+ * gemv_q / gemm_q NPU kernels (kernels/gemv_q/gemv_q.cc:14-73,
+ * kernels/gemm_q/gemm_q.cc:18-54). */
+int alv_gemv(alv_ctx* ctx, alv_handle h, int ntok, const void* x, int x_dtype, void* y,
+             int y_dtype, void* stream);
+
+/* Fused FFN on the registered slice: gate = bf16(Wg x), up = bf16(Wu x),
+ * act = bf16(act_fn(gate) * up), y = Wd act (fp32 accumulate).  x is
+ * (ntok, H), y is (ntok, H); 1 <= ntok <= 8.  For a tensor-parallel slice y
+ * is this device's partial sum (use ALV_F32 and all-reduce).  Replaces
+ * NpuRegistry::run_ffn_fused (npu.cpp:340-378) including its host partial
+ * sum, and the ffn_fused NPU design (kernels/ffn_fused/ffn_fused.py:28-328). */
+int alv_ffn(alv_ctx* ctx, alv_handle h, int ntok, const void* x, int x_dtype, void* y,
+            int y_dtype, void* stream);
+
+/* One FFN half-block of a decode layer with the layer glue fused in
+ * (runtime/py/model.py:782-806 with unit norm weights):
+ *   x      = down_in ? bf16(x_in + bf16(rmsnorm(bf16(down_in)))) : x_in
+ *   x_out  = x                         (if x_out != NULL)
+ *   down_out = Wd act(Wg, Wu; bf16(rmsnorm(x)))      (fp32, partial for TP)
+ * x_in/x_out bf16 (ntok, H); down_in/down_out fp32 (ntok, H); eps 1e-6. */
+int alv_ffn_layer(alv_ctx* ctx, alv_handle h, int ntok, const uint16_t* x_in,
+                  const float* down_in, uint16_t* x_out, float* down_out, void* stream);
+
+/* Final residual of an FFN stack: x_out = bf16(x_in + bf16(rmsnorm(bf16(down_in)))). */
+int alv_ffn_stack_finalize(alv_ctx* ctx, int ntok, int H, const uint16_t* x_in,
+                           const float* down_in, uint16_t* x_out, void* stream);
+
+/* ---- host-buffer convenience (synchronous, like NpuRegistry::run_gemv) ---- */
+
+/* Copy x from host memory, run, copy y back to host memory, synchronize and
+ * check status.  Mirrors npu.cpp:269-289 (memcpy to BO, sync, run, wait,
+ * sync back). */
+int alv_run_gemv(alv_ctx* ctx, alv_handle h, int ntok, const void* x_host, int x_dtype,
+                 void* y_host, int y_dtype);
+int alv_run_ffn(alv_ctx* ctx, alv_handle h, int ntok, const void* x_host, int x_dtype,
+                void* y_host, int y_dtype);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ALVEARE_B200_H */
