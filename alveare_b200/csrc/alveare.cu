@@ -214,9 +214,9 @@ int prepare_kernel(alv_ctx* ctx, K kernel, size_t smem) {
   return ALV_OK;
 }
 
-// Ring stages per warp that fit beside `other` bytes of shared memory (max 4).
+// Ring stages per warp that fit beside `other` bytes of shared memory (max 3).
 uint32_t ring_stages(size_t other) {
-  for (uint32_t nst = 4; nst >= 1; --nst)
+  for (uint32_t nst = 3; nst >= 1; --nst)
     if (ring_smem_bytes(nst) + other <= kMaxSmem) return nst;
   return 0;
 }

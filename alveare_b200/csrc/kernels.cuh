@@ -384,7 +384,7 @@ struct GemvParams {
   uint32_t nst;  // ring stages per warp
 };
 
-constexpr int kUnitsPerStage = 4;
+constexpr int kUnitsPerStage = 8;
 
 template <int UPS>
 __device__ __forceinline__ void ring_place(WarpRing<UPS>& ring, uint8_t* smem, int warp, uint32_t nst) {
@@ -414,6 +414,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 1) gemv_kernel(const GemvPa
   }
   WarpRing<kUnitsPerStage> ring;
   ring_place(ring, smem, warp, p.nst);
+  ring.status = p.status;
   ring.setup(p.m.units + static_cast<size_t>(u0) * kUnitBytes, u1 - u0, p.m.units, 0);
   ring.init_and_prime(lane);
 
@@ -512,6 +513,7 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32, 1) ffn_kernel(const FfnPara
   }
   WarpRing<kUnitsPerStage> ring;
   ring_place(ring, smem, warp, p.nst);
+  ring.status = p.status;
   ring.setup(p.gu.units + static_cast<size_t>(a0) * kUnitBytes, a1 - a0,
              p.dn.units + static_cast<size_t>(b0) * kUnitBytes, b1 - b0);
   ring.init_and_prime(lane);

@@ -163,48 +163,80 @@ struct WarpRing {
   uint8_t* ring;            // nst * kStageBytes (shared)
   uint64_t* bars;           // nst mbarriers (shared)
   uint64_t policy;
-  const uint8_t* seg[2];    // first unit of each segment's range
   uint32_t nst;             // number of stages
-  uint32_t n0;              // units in segment 0
-  uint32_t total;           // units in both segments
-  uint32_t ngroups;         // ceil(total / UPS)
-  uint32_t next_group;      // next group to issue
-  uint32_t stage, phase;    // consumer position
+  // producer (lane 0 issues; every lane keeps the same counters)
+  const uint8_t* p_src;     // source of the next unit to issue
+  const uint8_t* seg1;      // first unit of segment 1
+  const uint8_t* seg0_end;  // one past the last unit of each segment
+  const uint8_t* seg1_end;
+  uint32_t* status;         // device status word (bounds violations)
+  uint32_t p_left0;         // units of segment 0 not yet issued
+  uint32_t p_left;          // units not yet issued
+  uint32_t p_stage;         // stage the next group goes to
+  // consumer
+  uint32_t stage, phase;    // current stage and its parity
   uint32_t slot;            // units consumed in the current stage
-  uint32_t q;               // list position of the next unit to consume
+  uint32_t c_left;          // units not yet consumed
 
   __device__ void setup(const uint8_t* s0, uint32_t c0, const uint8_t* s1, uint32_t c1) {
-    seg[0] = s0;
-    seg[1] = s1;
-    n0 = c0;
-    total = c0 + c1;
-    ngroups = (total + UPS - 1) / UPS;
-    next_group = 0;
-    stage = phase = slot = q = 0;
+    p_src = c0 ? s0 : s1;
+    seg1 = s1;
+    seg0_end = s0 + static_cast<size_t>(c0) * kUnitBytes;
+    seg1_end = s1 + static_cast<size_t>(c1) * kUnitBytes;
+    p_left0 = c0;
+    p_left = c0 + c1;
+    c_left = c0 + c1;
+    p_stage = stage = phase = slot = 0;
   }
-  // lane 0: copy list units [g*UPS, min(g*UPS+UPS, total)) into stage `s`
-  __device__ __forceinline__ void issue(uint32_t g, uint32_t s) {
-    const uint32_t q0 = g * UPS;
-    const uint32_t q1 = q0 + UPS < total ? q0 + UPS : total;
-    uint8_t* dst = ring + s * kStageBytes;
-    mbar_arrive_expect_tx(&bars[s], (q1 - q0) * kUnitBytes);
-    if (q1 <= n0) {
-      bulk_g2s(dst, seg[0] + static_cast<size_t>(q0) * kUnitBytes, (q1 - q0) * kUnitBytes, &bars[s], policy);
-    } else if (q0 >= n0) {
-      bulk_g2s(dst, seg[1] + static_cast<size_t>(q0 - n0) * kUnitBytes, (q1 - q0) * kUnitBytes, &bars[s], policy);
-    } else {
-      bulk_g2s(dst, seg[0] + static_cast<size_t>(q0) * kUnitBytes, (n0 - q0) * kUnitBytes, &bars[s], policy);
-      bulk_g2s(dst + (n0 - q0) * kUnitBytes, seg[1], (q1 - n0) * kUnitBytes, &bars[s], policy);
+  // lane 0: copy the next min(UPS, p_left) list units into stage p_stage.
+  // Every copy is checked against the end of its segment; a copy that would
+  // leave it is not issued and reported (the consumer's wait then times out).
+  __device__ __forceinline__ void issue_next() {
+    const uint32_t n = p_left < UPS ? p_left : UPS;
+    uint8_t* dst = ring + p_stage * kStageBytes;
+    uint64_t* bar = &bars[p_stage];
+    if (n <= p_left0 || p_left0 == 0) {
+      const uint8_t* end = p_left0 ? seg0_end : seg1_end;
+      if (p_src + n * kUnitBytes > end) {
+        atomicOr(status, kStatusBadLaunch);
+        return;
+      }
+      mbar_arrive_expect_tx(bar, n * kUnitBytes);
+      bulk_g2s(dst, p_src, n * kUnitBytes, bar, policy);
+    } else {  // the group straddles the end of segment 0
+      if (p_src + p_left0 * kUnitBytes > seg0_end || seg1 + (n - p_left0) * kUnitBytes > seg1_end) {
+        atomicOr(status, kStatusBadLaunch);
+        return;
+      }
+      mbar_arrive_expect_tx(bar, n * kUnitBytes);
+      bulk_g2s(dst, p_src, p_left0 * kUnitBytes, bar, policy);
+      bulk_g2s(dst + p_left0 * kUnitBytes, seg1, (n - p_left0) * kUnitBytes, bar, policy);
     }
   }
+  // every lane: advance the producer counters past one issued group
+  __device__ __forceinline__ void advance_producer() {
+    const uint32_t n = p_left < UPS ? p_left : UPS;
+    if (n < p_left0) {          // still inside segment 0
+      p_src += n * kUnitBytes;
+      p_left0 -= n;
+    } else if (p_left0 > 0) {   // reached or crossed the end of segment 0
+      p_src = seg1 + (n - p_left0) * kUnitBytes;
+      p_left0 = 0;
+    } else {                    // inside segment 1
+      p_src += n * kUnitBytes;
+    }
+    p_left -= n;
+    if (++p_stage == nst) p_stage = 0;
+  }
   __device__ void init_and_prime(int lane) {
-    const uint32_t n = ngroups < nst ? ngroups : nst;
     if (lane == 0) {
       for (uint32_t s = 0; s < nst; ++s) mbar_init(&bars[s], 1);
       fence_mbar_init();
-      for (uint32_t g = 0; g < n; ++g) issue(g, g);
     }
-    next_group = n;
+    for (uint32_t s = 0; s < nst && p_left; ++s) {
+      if (lane == 0) issue_next();
+      advance_producer();
+    }
     __syncwarp();
   }
   __device__ __forceinline__ bool wait_stage() {  // warp-uniform result
@@ -213,21 +245,24 @@ struct WarpRing {
   __device__ __forceinline__ const uint8_t* unit_ptr() const {
     return ring + stage * kStageBytes + slot * kUnitBytes;
   }
-  // Units left in the current stage.
+  // Units left in the current stage (its group holds min(UPS, units left at
+  // the group's start) units).
   __device__ __forceinline__ uint32_t stage_left() const {
-    const uint32_t end = (q - slot) + UPS;
-    return (end < total ? end : total) - q;
+    const uint32_t at_start = c_left + slot;
+    return (at_start < UPS ? at_start : UPS) - slot;
   }
   // Consume `n` units of the current stage; refill the stage once finished.
   // The refill overwrites data this warp already read into registers and used,
   // so no proxy fence is needed (only generic-proxy writes need one).
   __device__ __forceinline__ void consume(uint32_t n, int lane) {
-    q += n;
+    c_left -= n;
     slot += n;
-    if (slot == UPS || q == total) {
+    if (slot == UPS || c_left == 0) {
       __syncwarp();
-      if (lane == 0 && next_group < ngroups) issue(next_group, stage);
-      ++next_group;
+      if (p_left) {
+        if (lane == 0) issue_next();
+        advance_producer();
+      }
       slot = 0;
       if (++stage == nst) {
         stage = 0;
@@ -235,13 +270,19 @@ struct WarpRing {
       }
     }
   }
-  // After an error: wait (bounded) for every stage still being filled, i.e.
-  // groups [consumed, min(consumed + nst, ngroups)).
+  // After an error: wait (bounded) for every stage that was issued and not
+  // yet consumed, starting with the current one.
   __device__ void drain() {
-    const uint32_t consumed = q / UPS;
-    const uint32_t end = consumed + nst < ngroups ? consumed + nst : ngroups;
-    for (uint32_t g = consumed; g < end; ++g)
-      (void)mbar_wait_bounded(&bars[g % nst], (g / nst) & 1);
+    const uint32_t issued_not_consumed_units = c_left + slot - p_left;
+    uint32_t groups = (issued_not_consumed_units + UPS - 1) / UPS;
+    uint32_t s = stage, ph = phase;
+    for (; groups; --groups) {
+      (void)mbar_wait_bounded(&bars[s], ph);
+      if (++s == nst) {
+        s = 0;
+        ph ^= 1;
+      }
+    }
   }
 };
 

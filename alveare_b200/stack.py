@@ -1,0 +1,114 @@
+"""Decode-time FFN stack: L fused-FFN half-blocks with the layer glue fused in,
+optionally tensor-parallel over the intermediate dimension.
+
+This is the decode loop's FFN call site of the reference
+(runtime/cpp/src/model.cpp:404, runtime/py/model.py:782-806) moved onto the
+GPU: per layer ``x2 = rmsnorm(x)``, ``down = FFN(x2)``,
+``x = x + rmsnorm(down)`` (unit norm weights), with every step on the device.
+Tensor parallelism splits each FFN's intermediate dimension over the ranks
+(the reference's I-split across AIE cores, kernels/ffn_fused/ffn_fused.py:46-60,
+lifted to GPUs); the per-layer partial down projections are summed with one
+NCCL all-reduce of H fp32 values (the reference's host partial sum,
+runtime/cpp/src/npu.cpp:360-377).  A step is captured once into a CUDA graph
+and replayed.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from .ops import FusedFFNWeight
+
+
+class FFNStack:
+    """Resident FFN stack on one GPU (one rank of a tensor-parallel group).
+
+    layers: list of (gate, up, down) packed Q4 buffers in the reference layout
+    (torch CUDA uint8 tensors or host numpy arrays).  With ``world > 1`` this
+    rank keeps intermediate slice [rank*I/world, (rank+1)*I/world) and
+    ``torch.distributed`` (NCCL) must be initialized.
+    """
+
+    def __init__(self, H: int, I: int, device: int = 0, rank: int = 0, world: int = 1,
+                 activation: str = "gelu"):
+        if I % (32 * world):
+            raise ValueError("I must split into 32-aligned slices over the ranks")
+        self.H, self.I, self.device, self.rank, self.world = H, I, device, rank, world
+        self.activation = activation
+        self.i_begin = rank * I // world
+        self.i_end = (rank + 1) * I // world
+        self.layers: list[FusedFFNWeight] = []
+        dev = torch.device("cuda", device)
+        self.x = [torch.zeros(H, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        self.down = [torch.zeros(H, dtype=torch.float32, device=dev) for _ in range(2)]
+        self.out = torch.zeros(H, dtype=torch.bfloat16, device=dev)
+        self.graph = None
+        self.stream = torch.cuda.Stream(device=dev)
+
+    @property
+    def ctx(self):
+        return _lib.context(self.device)
+
+    def add_layer(self, gate, up, down) -> None:
+        self.layers.append(FusedFFNWeight(gate, up, down, self.H, self.I, self.activation, device=self.device,
+                                          i_begin=self.i_begin, i_end=self.i_end))
+
+    def weight_bytes(self) -> int:
+        """Algorithmic weight bytes of the whole stack (all ranks): 18 B per 32 weights."""
+        return len(self.layers) * 3 * self.H * self.I // 32 * 18
+
+    # -- one decode step --------------------------------------------------
+    def _enqueue(self, layers_only: bool = False) -> int:
+        """Enqueue one step on the current stream; returns kernels launched."""
+        ctx = self.ctx
+        st = torch.cuda.current_stream(self.device).cuda_stream
+        n = 0
+        L = len(self.layers)
+        for l, w in enumerate(self.layers):
+            x_in, x_out = self.x[l % 2], self.x[(l + 1) % 2]
+            down_in = self.down[(l + 1) % 2].data_ptr() if l else None
+            ctx.check(ctx.lib.alv_ffn_layer(ctx.ptr, w.handle, 1, x_in.data_ptr(), down_in, x_out.data_ptr(),
+                                            self.down[l % 2].data_ptr(), st), "alv_ffn_layer")
+            n += 1
+            if self.world > 1 and not layers_only:
+                torch.distributed.all_reduce(self.down[l % 2])
+        if not layers_only:
+            ctx.check(ctx.lib.alv_ffn_stack_finalize(ctx.ptr, 1, self.H, self.x[L % 2].data_ptr(),
+                                                     self.down[(L - 1) % 2].data_ptr(), self.out.data_ptr(), st),
+                      "alv_ffn_stack_finalize")
+            n += 1
+        return n
+
+    def capture(self, layers_only: bool = False) -> torch.cuda.CUDAGraph:
+        """Capture one step (input self.x[0] -> output self.out) into a graph."""
+        with torch.cuda.stream(self.stream):
+            self._enqueue(layers_only)          # warm-up outside capture
+        self.stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=self.stream):
+            self.launches = self._enqueue(layers_only)
+        return g
+
+    def prepare(self) -> None:
+        if self.graph is None:
+            self.graph = self.capture()
+
+    def replay(self) -> None:
+        self.graph.replay()
+
+    def forward(self, x_host: torch.Tensor, y_host: torch.Tensor) -> None:
+        """Public decode call with host buffers: copy x (bf16, pinned host) in,
+        run the stack, copy the new residual stream back into y_host."""
+        self.prepare()
+        with torch.cuda.stream(self.stream):
+            self.x[0].copy_(x_host, non_blocking=True)
+            self.graph.replay()
+            y_host.copy_(self.out, non_blocking=True)
+        self.stream.synchronize()
+        self.ctx.sync_status(self.stream.cuda_stream)
+
+    def release(self) -> None:
+        """Drop captured graphs (before destroying a process group)."""
+        self.graph = None
