@@ -52,6 +52,7 @@ SIGNATURES = {
     "alv_ffn_stack_finalize": (_i, [_vp, _i, _i, _vp, _vp, _vp, _vp]),
     "alv_run_gemv": (_i, [_vp, _u32, _i, _vp, _i, _vp, _i]),
     "alv_run_ffn": (_i, [_vp, _u32, _i, _vp, _i, _vp, _i]),
+    "alv_gemv_noalloc": (_i, [_vp, _u32, _i, _vp, _i, _vp, _i, _vp]),
 }
 
 _lock = threading.Lock()

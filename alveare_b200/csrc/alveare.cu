@@ -761,3 +761,85 @@ int alv_run_ffn(alv_ctx* ctx, alv_handle h, int ntok, const void* x_host, int x_
 }
 
 }  // extern "C"
+
+// ===========================================================================
+// Allocation-free gemv.
+//
+// Some callers cannot allocate device memory while they run: a decode loop
+// whose GPU memory budget is fixed at start-up (every byte is handed to a
+// KV cache or another pool), a host runtime that owns the device allocator
+// and forbids others from calling cudaMalloc, or code that must not trigger
+// the implicit device synchronization a cudaMalloc/cudaFree can cause.
+// alv_gemv may grow the context's scratch arena (cudaMalloc) the first time a
+// larger problem arrives; alv_gemv_noalloc never does.  Its split-K workspace
+// and arrival counters live in the fixed array below, which every GPU that
+// loads this library holds until the process exits.
+// ===========================================================================
+namespace {
+constexpr uint32_t kNoAllocMaxTokens = 4;                 // tokens per call
+constexpr uint32_t kNoAllocMaxRowTiles = 16384;           // N <= 262,144 rows
+constexpr uint32_t kNoAllocMaxWarps = 148 * kWarpsPerCta; // one 16-warp CTA per SM of a B200
+constexpr size_t kNoAllocWsFloats = static_cast<size_t>(kNoAllocMaxWarps) * 2 * kNoAllocMaxTokens * 16;
+constexpr size_t kNoAllocCounterBytes = static_cast<size_t>(kNoAllocMaxRowTiles) * 4;
+constexpr size_t kNoAllocBytes = kNoAllocCounterBytes + kNoAllocWsFloats * 4;  // 1,277,952 bytes
+}  // namespace
+
+// [counters: kNoAllocMaxRowTiles x u32][workspace: kNoAllocWsFloats x f32]
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {};  // device address of g_noalloc_scratch, per device
+
+// Once per device, with that device current: look up the device address of
+// the static array (its host-side name is only a stand-in, not a device
+// pointer).
+int noalloc_scratch(alv_ctx* ctx, uint8_t** out) {
+  if (ctx->device < 0 || ctx->device >= 64) return fail(ctx, ALV_ERR_UNSUPPORTED, "gemv_noalloc: device index >= 64");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[ctx->device]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(ctx, ALV_ERR_CUDA, std::string("gemv_noalloc: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+    g_noalloc_addr[ctx->device] = p;
+  }
+  *out = static_cast<uint8_t*>(g_noalloc_addr[ctx->device]);
+  return ALV_OK;
+}
+}  // namespace
+
+extern "C" int alv_gemv_noalloc(alv_ctx* ctx, alv_handle h, int ntok, const void* x, int x_dtype, void* y,
+                                int y_dtype, void* stream) {
+  if (!ctx || !x || !y || !valid_dtype(x_dtype) || !valid_dtype(y_dtype))
+    return fail(ctx, ALV_ERR_ARG, "gemv_noalloc: bad argument");
+  Weight* w = get_weight(ctx, h, 1);
+  if (!w) return fail(ctx, ALV_ERR_HANDLE, "gemv_noalloc: invalid handle (not a gemv weight)");
+  int rc = set_device(ctx);
+  if (rc) return rc;
+  const bool split = x_dtype == ALV_F32;
+  const uint32_t ncols = pow2_ceil(static_cast<uint32_t>(split ? 2 * ntok : ntok));
+  if (ntok < 1 || ntok > static_cast<int>(kNoAllocMaxTokens))
+    return fail(ctx, ALV_ERR_UNSUPPORTED, "gemv_noalloc: ntok must be 1.." + std::to_string(kNoAllocMaxTokens));
+  if (w->a.m.RT > kNoAllocMaxRowTiles)
+    return fail(ctx, ALV_ERR_UNSUPPORTED, "gemv_noalloc: N must be <= " + std::to_string(kNoAllocMaxRowTiles * 16));
+  if (static_cast<uint32_t>(ctx->num_sms) * kWarpsPerCta > kNoAllocMaxWarps)
+    return fail(ctx, ALV_ERR_UNSUPPORTED, "gemv_noalloc: GPU has more SMs than the static workspace covers");
+  if (ws_floats(ctx, w->a.m, ntok) > kNoAllocWsFloats)
+    return fail(ctx, ALV_ERR_UNSUPPORTED, "gemv_noalloc: split-K workspace exceeds the static array");
+  uint8_t* base = nullptr;
+  if ((rc = noalloc_scratch(ctx, &base))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // The array keeps the previous call's contents: the arrival counters this
+  // call uses must start at zero.
+  ALV_CUDA(ctx, cudaMemsetAsync(base, 0, static_cast<size_t>(w->a.m.RT) * 4, st));
+  GemvParams p{};
+  p.m = w->a.m;
+  p.x = XSrc{x, x_dtype == ALV_BF16, ntok, w->a.cols, w->a.cols};
+  p.epi = RowsEpi{y_dtype == ALV_F32 ? static_cast<float*>(y) : nullptr,
+                  y_dtype == ALV_BF16 ? static_cast<uint16_t*>(y) : nullptr, w->a.rows, w->a.rows,
+                  w->a.m.scale_mul};
+  p.fx = Fixup{reinterpret_cast<float*>(base + kNoAllocCounterBytes), reinterpret_cast<uint32_t*>(base)};
+  p.status = status_ptr(ctx);
+  return launch_gemv(ctx, p, split, ncols, st);
+}

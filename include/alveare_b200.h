@@ -143,6 +143,23 @@ int alv_ffn_layer(alv_ctx* ctx, alv_handle h, int ntok, const uint16_t* x_in,
 int alv_ffn_stack_finalize(alv_ctx* ctx, int ntok, int H, const uint16_t* x_in,
                            const float* down_in, uint16_t* x_out, void* stream);
 
+/* Allocation-free gemv: same arithmetic and arguments as alv_gemv, for
+ * callers that must not allocate device memory while they run (a decode
+ * loop with a fixed GPU memory budget, a host runtime that owns the device
+ * allocator, code that cannot afford the device synchronization of
+ * cudaMalloc/cudaFree).  alv_gemv may grow the context's scratch arena on
+ * the first larger call; this entry point never allocates: its split-K
+ * workspace and counters live in a static device array of 1,277,952 bytes
+ * that every GPU loading the library holds until process exit.  Limits:
+ * ntok <= 4, N <= 262,144 rows, GPUs with <= 148 SMs; larger requests return
+ * ALV_ERR_UNSUPPORTED.  The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress), so make that first call before any
+ * stream capture.  All calls share the one array: calls that overlap on the
+ * GPU (different streams, or concurrent host threads) race and must be
+ * serialized by the caller.  No counterpart in the reference. */
+int alv_gemv_noalloc(alv_ctx* ctx, alv_handle h, int ntok, const void* x, int x_dtype, void* y,
+                     int y_dtype, void* stream);
+
 /* ---- host-buffer convenience (synchronous, like NpuRegistry::run_gemv) ---- */
 
 /* Copy x from host memory, run, copy y back to host memory, synchronize and
