@@ -50,6 +50,7 @@ struct alv_ctx {
   void* io = nullptr;                            // device staging for host-buffer calls
   size_t io_bytes = 0;
   cudaStream_t stream = nullptr;                 // internal stream (loads, host calls)
+  unsigned long long* trace = nullptr;           // optional FFN phase timestamps
 };
 
 namespace {
@@ -230,7 +231,7 @@ int launch_gemv_t(alv_ctx* ctx, GemvParams p, cudaStream_t st) {
   auto k = gemv_kernel<NCOLS, SPLIT, FAST>;
   int rc = prepare_kernel(ctx, k, smem);
   if (rc) return rc;
-  k<<<ctx->num_sms, kWarpsPerCta * 32, smem, st>>>(p);
+  k<<<ctx->num_sms, kThreadsPerCta, smem, st>>>(p);
   ALV_CUDA(ctx, cudaGetLastError());
   return ALV_OK;
 }
@@ -264,14 +265,19 @@ template <int NT, bool SPLIT, bool FAST>
 int launch_ffn_t(alv_ctx* ctx, FfnParams p, cudaStream_t st) {
   constexpr int NCA = SPLIT ? 2 * NT : NT;
   size_t other = std::max(frag_bytes(p.gu.KT, NCA), frag_bytes(p.dn.KT, NT)) + 32 * sizeof(float);
-  if (p.glue) other += static_cast<size_t>(p.ntok) * p.H * sizeof(float);
+  if (p.glue) {
+    const size_t v = static_cast<size_t>(p.ntok) * p.H;
+    other += v * sizeof(float);                                  // tmp
+    if (p.glue_tma) other += v * 2 + (p.down_in ? v * 4 : 0);    // raw inputs
+  }
+  other += 16;                                                   // input mbarrier
   p.nst = ring_stages(other);
   if (!p.nst) return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn: H or I too large for the shared-memory fragment stage");
   const size_t smem = ring_smem_bytes(p.nst) + other;
   auto k = ffn_kernel<NT, SPLIT, FAST>;
   int rc = prepare_kernel(ctx, k, smem);
   if (rc) return rc;
-  k<<<ctx->num_sms, kWarpsPerCta * 32, smem, st>>>(p);
+  k<<<ctx->num_sms, kThreadsPerCta, smem, st>>>(p);
   ALV_CUDA(ctx, cudaGetLastError());
   return ALV_OK;
 }
@@ -343,13 +349,14 @@ struct FfnIo {
 
 int do_ffn(alv_ctx* ctx, Weight* w, int ntok, const FfnIo& io, cudaStream_t st) {
   if (ntok < 1 || ntok > 8) return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn: ntok must be 1..8");
+  if (io.glue && w->H > 32u * kConsumerWarps * kGlueRegs)
+    return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn_layer: H must be <= " + std::to_string(32u * kConsumerWarps * kGlueRegs));
   const bool split = !io.glue && io.x_dtype == ALV_F32;
   const uint32_t nt = pow2_ceil(static_cast<uint32_t>(ntok));
   if (w->a.m.RT + w->b.m.RT > kMaxCounters) return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn: too large");
-  const uint32_t act_ld = static_cast<uint32_t>(align_up(w->I, 64));
   const size_t wsA = align_up(ws_floats(ctx, w->a.m, ntok) * 4, 256);
   const size_t wsB = align_up(ws_floats(ctx, w->b.m, ntok) * 4, 256);
-  const size_t actb = align_up(static_cast<size_t>(ntok) * act_ld * 2, 256);
+  const size_t actb = align_up(frag_bytes(w->b.m.KT, static_cast<int>(nt)), 256);
   int rc = ensure_scratch(ctx, wsA + wsB + actb);
   if (rc) return rc;
   uint8_t* wk = work_ptr(ctx);
@@ -367,12 +374,14 @@ int do_ffn(alv_ctx* ctx, Weight* w, int ntok, const FfnIo& io, cudaStream_t st) 
   p.x_out = io.x_out;
   p.eps = 1e-6f;
   p.out = RowsEpi{io.y32, io.y16, w->H, w->H, w->b.m.scale_mul};
-  p.act = reinterpret_cast<uint16_t*>(wk + wsA + wsB);
-  p.act_ld = act_ld;
+  p.act = wk + wsA + wsB;
   p.fxA = Fixup{reinterpret_cast<float*>(wk), counters_ptr(ctx)};
   p.fxB = Fixup{reinterpret_cast<float*>(wk + wsA), counters_ptr(ctx) + w->a.m.RT};
   p.bar = bar_ptr(ctx);
   p.status = status_ptr(ctx);
+  p.trace = ctx->trace;
+  auto aligned16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  p.glue_tma = io.glue && aligned16(io.x_in) && (!io.down_in || aligned16(io.down_in));
   return launch_ffn(ctx, p, split, nt, st);
 }
 
@@ -601,6 +610,12 @@ int alv_ffn_set_activation(alv_ctx* ctx, alv_handle h, int act) {
   return ALV_OK;
 }
 
+int alv_set_trace(alv_ctx* ctx, uint64_t* trace) {
+  if (!ctx) return ALV_ERR_ARG;
+  ctx->trace = reinterpret_cast<unsigned long long*>(trace);
+  return ALV_OK;
+}
+
 int alv_weight_info(alv_ctx* ctx, alv_handle h, int64_t* info) {
   if (!ctx || !info) return ALV_ERR_ARG;
   Weight* w = get_weight(ctx, h, 0);
@@ -778,7 +793,7 @@ int alv_run_ffn(alv_ctx* ctx, alv_handle h, int ntok, const void* x_host, int x_
 namespace {
 constexpr uint32_t kNoAllocMaxTokens = 4;                 // tokens per call
 constexpr uint32_t kNoAllocMaxRowTiles = 16384;           // N <= 262,144 rows
-constexpr uint32_t kNoAllocMaxWarps = 148 * kWarpsPerCta; // one 16-warp CTA per SM of a B200
+constexpr uint32_t kNoAllocMaxWarps = 2368;               // participating warps covered (>= 148 SMs x 15)
 constexpr size_t kNoAllocWsFloats = static_cast<size_t>(kNoAllocMaxWarps) * 2 * kNoAllocMaxTokens * 16;
 constexpr size_t kNoAllocCounterBytes = static_cast<size_t>(kNoAllocMaxRowTiles) * 4;
 constexpr size_t kNoAllocBytes = kNoAllocCounterBytes + kNoAllocWsFloats * 4;  // 1,277,952 bytes

@@ -32,7 +32,7 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
 }
 
 // ---------------------------------------------------------------------------
-// mbarrier + bulk copy (global -> shared through the TMA engine, no multicast)
+// mbarrier + 1-D bulk copy (global -> this CTA's shared memory through the TMA engine)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
@@ -117,6 +117,24 @@ __device__ __forceinline__ uint4 lds128(const void* p) {
 __device__ __forceinline__ uint2 lds64(const void* p) {
   uint2 v;
   asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(smem_u32(p)));
+  return v;
+}
+
+// Loads at a 32-bit shared-space address plus a compile-time byte offset
+// (folded into the instruction's immediate).
+template <int OFF>
+__device__ __forceinline__ uint4 lds128_at(uint32_t saddr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4+%5];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(saddr), "n"(OFF));
+  return v;
+}
+
+template <int OFF>
+__device__ __forceinline__ uint2 lds64_at(uint32_t saddr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2+%3];" : "=r"(v.x), "=r"(v.y) : "r"(saddr), "n"(OFF));
   return v;
 }
 

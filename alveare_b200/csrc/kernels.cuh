@@ -10,7 +10,7 @@
 
 namespace alv {
 
-constexpr int kWarpsPerCta = 16;
+constexpr int kWarpsPerCta = kConsumerWarps;  // consumer warps per CTA (one more warp produces)
 
 // ===========================================================================
 // GPU quantizer: restates tools/convert/gemv_q_convert.py:5-85.
@@ -307,10 +307,17 @@ __device__ __forceinline__ float swiglu_ref(float g, float u) {
   return __fmul_rn(__fmul_rn(g, s), u);
 }
 
+// Byte offset of value (column n, k) in the B-fragment layout (stage_frags).
+__device__ __forceinline__ uint32_t frag_offset(uint32_t ncols, uint32_t n, uint32_t k) {
+  const uint32_t kt = k >> 6, r = k & 63, j = r >> 4, c = r & 15;
+  const uint32_t t4 = (c & 7) >> 1, reg = c >> 3, half = c & 1;
+  return ((kt * ncols + n) * 4 + t4) * 32 + j * 8 + reg * 4 + half * 2;
+}
+
 struct GateUpEpi {  // tile rows 0-7 gate, 8-15 up of the same 8 intermediate indices
-  uint16_t* act;
+  uint8_t* act;     // fragment-order act for the down projection (ncb columns)
   uint32_t I;
-  uint32_t ld;
+  uint32_t ncb;
   float sm;
   int fn;
   __device__ __forceinline__ void apply(uint32_t r, int g, int tok, float vg, float vg8) const {
@@ -318,7 +325,7 @@ struct GateUpEpi {  // tile rows 0-7 gate, 8-15 up of the same 8 intermediate in
     if (i >= I) return;
     const float gate = bf16_round(vg * sm), up = bf16_round(vg8 * sm);
     const float a = fn == 0 ? geglu_ref(gate, up) : swiglu_ref(gate, up);
-    act[static_cast<uint64_t>(tok) * ld + i] = bf16_bits_rn(a);
+    *reinterpret_cast<uint16_t*>(act + frag_offset(ncb, static_cast<uint32_t>(tok), i)) = bf16_bits_rn(a);
   }
 };
 
@@ -326,26 +333,24 @@ struct GateUpEpi {  // tile rows 0-7 gate, 8-15 up of the same 8 intermediate in
 // Grid-wide barrier (sense by generation counter), bounded wait.
 // ===========================================================================
 struct GridBar {
-  uint32_t count;
-  uint32_t gen;
+  unsigned long long count;  // monotonically increasing arrivals (never wraps)
 };
 
+// One atomic per CTA: the k-th use of the barrier completes when the counter
+// reaches k * nblocks; waiters poll the counter itself.  Correct across
+// launches because every launch uses it a whole number of times with the
+// same grid, so the counter always resumes at a multiple of nblocks.
 __device__ bool grid_barrier(GridBar* gb, uint32_t nblocks, uint32_t* status) {
-  __syncthreads();
+  consumers_sync();
   int ok = 1;
   if (threadIdx.x == 0) {
-    volatile uint32_t* vgen = &gb->gen;
-    const uint32_t gen = *vgen;
     __threadfence();
-    const uint32_t arrived = atomicAdd(&gb->count, 1u);
-    if (arrived == nblocks - 1) {
-      atomicExch(&gb->count, 0u);
-      __threadfence();
-      atomicAdd(&gb->gen, 1u);
-    } else {
+    const unsigned long long arrived = atomicAdd(&gb->count, 1ull);
+    const unsigned long long target = (arrived / nblocks + 1) * nblocks;
+    volatile unsigned long long* vc = &gb->count;
+    if (*vc < target) {
       const unsigned long long t0 = globaltimer_ns();
-      while (*vgen == gen) {
-        __nanosleep(64);
+      while (*vc < target) {
         if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
           atomicOr(status, kStatusGridTimeout);
           ok = 0;
@@ -355,10 +360,25 @@ __device__ bool grid_barrier(GridBar* gb, uint32_t nblocks, uint32_t* status) {
     }
     __threadfence();
   }
-  return __syncthreads_and(ok) != 0;
+  return consumers_and(ok != 0);
 }
 
-// Block-wide sum (all threads get the result); red holds >= 32 floats.
+// Sum over the consumer threads (all of them get the result); red holds >= 32
+// floats.  Fixed order, so every CTA computes the identical value.
+__device__ float consumers_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  consumers_sync();
+  if (lane == 0) red[warp] = v;
+  consumers_sync();
+  float s = 0.f;
+  for (int i = 0; i < kConsumerWarps; ++i) s += red[i];
+  consumers_sync();
+  return s;
+}
+
+// Single-CTA block sum for the finalize kernel (blockDim.x threads).
 __device__ float block_sum(float v, float* red) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
 #pragma unroll
@@ -367,7 +387,7 @@ __device__ float block_sum(float v, float* red) {
   if (lane == 0) red[warp] = v;
   __syncthreads();
   float s = 0.f;
-  for (int i = 0; i < nw; ++i) s += red[i];  // fixed order: identical in every CTA
+  for (int i = 0; i < nw; ++i) s += red[i];
   __syncthreads();
   return s;
 }
@@ -385,44 +405,42 @@ struct GemvParams {
 };
 
 constexpr int kUnitsPerStage = 8;
+constexpr int kThreadsPerCta = (kConsumerWarps + 1) * 32;  // consumer warps + 1 producer warp
+using Shape = RingShape<kUnitsPerStage>;
 
-template <int UPS>
-__device__ __forceinline__ void ring_place(WarpRing<UPS>& ring, uint8_t* smem, int warp, uint32_t nst) {
-  constexpr size_t stage_bytes = WarpRing<UPS>::kStageBytes;
-  ring.nst = nst;
-  ring.ring = smem + static_cast<size_t>(warp) * nst * stage_bytes;
-  ring.bars = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(kWarpsPerCta) * nst * stage_bytes) +
-              warp * nst;
-  ring.policy = l2_policy_evict_first();
-}
-
-__host__ __device__ constexpr size_t ring_smem_bytes(uint32_t nst) {
-  return static_cast<size_t>(kWarpsPerCta) * nst * (kUnitsPerStage * kUnitBytes + 8);
-}
+__host__ __device__ constexpr size_t ring_smem_bytes(uint32_t nst) { return Shape::smem_bytes(nst); }
 
 template <int NCOLS, bool SPLIT, bool FAST>
-__global__ void __launch_bounds__(kWarpsPerCta * 32, 1) gemv_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(kThreadsPerCta, 1) gemv_kernel(const GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t gw = participant_index(blockIdx.x, warp, gridDim.x);
   const uint64_t U = static_cast<uint64_t>(p.m.RT) * p.m.KT;
   const uint64_t W = effective_warps(static_cast<uint64_t>(gridDim.x) * kWarpsPerCta, U, p.m.KT);
+  Shape::init_barriers(smem, p.nst);
+  __syncthreads();
+  // Consumer warp c of this CTA (the producer's lane c serves it).
+  const int c = warp < kConsumerWarps ? warp : lane;
+  const uint32_t gw = participant_index(blockIdx.x, static_cast<uint32_t>(c), gridDim.x);
   uint32_t u0 = 0, u1 = 0;
-  if (gw < W) {
+  if (c < kConsumerWarps && gw < W) {
     u0 = static_cast<uint32_t>(range_start(gw, U, W));
     u1 = static_cast<uint32_t>(range_start(gw + 1, U, W));
   }
-  WarpRing<kUnitsPerStage> ring;
-  ring_place(ring, smem, warp, p.nst);
-  ring.status = p.status;
-  ring.setup(p.m.units + static_cast<size_t>(u0) * kUnitBytes, u1 - u0, p.m.units, 0);
-  ring.init_and_prime(lane);
-
+  if (warp == kConsumerWarps) {
+    const WorkList wl{p.m.units + static_cast<size_t>(u0) * kUnitBytes, p.m.units, u1 - u0, 0};
+    producer_wait_release();
+    produce<kUnitsPerStage>(smem, p.nst, wl, l2_policy_evict_first(), p.status);
+    return;
+  }
+  ConsumerRing<kUnitsPerStage> ring;
+  ring.setup(smem, p.nst, warp, u1 - u0);
   uint8_t* xs = smem + ring_smem_bytes(p.nst);
   stage_frags<NCOLS, SPLIT>(xs, p.m.KT, p.x);
-  __syncthreads();
-  consume_range<NCOLS, SPLIT, FAST>(ring, p.m, u0, u1, xs, p.fx, gw, static_cast<uint32_t>(W), p.x.ntok,
-                                    p.epi, p.status);
+  consumers_sync();
+  consumers_release_producer();
+  if (!consume_range<NCOLS, SPLIT, FAST>(ring, p.m, u0, u1, xs, p.fx, gw, static_cast<uint32_t>(W), p.x.ntok,
+                                         p.epi, p.status))
+    ring.drain(lane);
 }
 
 // ===========================================================================
@@ -444,107 +462,189 @@ struct FfnParams {
   uint16_t* x_out;
   float eps;
   RowsEpi out;          // down projection output
-  uint16_t* act;        // scratch [ntok][act_ld]
-  uint32_t act_ld;
+  uint8_t* act;         // scratch: act in B-fragment order, frag_bytes(dn.KT, NT) bytes
   Fixup fxA, fxB;
   GridBar* bar;
   uint32_t* status;
   uint32_t nst;  // ring stages per warp
+  unsigned long long* trace;  // optional: [gridDim.x][16] phase timestamps (ns)
+  int glue_tma;          // glue inputs 16-byte aligned: fetch them with bulk copies
 };
+
+// Phase timestamps of one CTA (thread 0): 0 start, 1 prologue staged, 2 phase A
+// done (all warps), 3 grid barrier passed, 4 act staged, 5 phase B done.
+__device__ __forceinline__ void trace_mark(unsigned long long* trace, int i) {
+  if (trace && threadIdx.x == 0) trace[blockIdx.x * 16 + i] = globaltimer_ns();
+}
 
 // Glue prologue: build x = bf16(x_in + bf16(rmsnorm(bf16(down_in)))) and
 // xn = bf16(rmsnorm(x)) per token into tmp[ntok][H] (fp32 holding bf16 values).
-__device__ void ffn_glue_prologue(const FfnParams& p, float* tmp, float* red) {
+// Each consumer thread keeps its share of H in registers, so every global
+// load of a token is in flight at once.  H <= 32 * kConsumerWarps * kGlueRegs.
+constexpr int kGlueRegs = 16;
+
+// x_src / d_src: the inputs in global or shared memory (d_src may be null).
+__device__ void ffn_glue_prologue(const FfnParams& p, const uint16_t* x_src, const float* d_src, float* tmp,
+                                  float* red) {
+  constexpr uint32_t NTHR = kConsumerWarps * 32;
   const uint32_t H = p.H;
   const float hf = static_cast<float>(H);  // np.mean divides the float32 sum by n
   for (int tok = 0; tok < p.ntok; ++tok) {
-    float* xt = tmp + static_cast<size_t>(tok) * H;
-    const uint16_t* xi = p.x_in + static_cast<size_t>(tok) * H;
-    if (p.down_in) {
-      const float* di = p.down_in + static_cast<size_t>(tok) * H;
-      float ss = 0.f;
-      for (uint32_t h = threadIdx.x; h < H; h += blockDim.x) {
-        const float d = bf16_round(di[h]);
-        xt[h] = d;
-        ss = fmaf(d, d, ss);
-      }
-      ss = block_sum(ss, red);
-      const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, hf), p.eps)));
-      for (uint32_t h = threadIdx.x; h < H; h += blockDim.x) {
-        const float dn = bf16_round(xt[h] * inv);
-        xt[h] = bf16_round(bf16_bits_to_f32(xi[h]) + dn);
-      }
-    } else {
-      for (uint32_t h = threadIdx.x; h < H; h += blockDim.x) xt[h] = bf16_bits_to_f32(xi[h]);
+    const uint16_t* xi = x_src + static_cast<size_t>(tok) * H;
+    const float* di = d_src ? d_src + static_cast<size_t>(tok) * H : nullptr;
+    float xv[kGlueRegs], dv[kGlueRegs];
+#pragma unroll
+    for (int i = 0; i < kGlueRegs; ++i) {
+      const uint32_t h = threadIdx.x + i * NTHR;
+      xv[i] = h < H ? bf16_bits_to_f32(xi[h]) : 0.f;
+      dv[i] = (di && h < H) ? bf16_round(di[h]) : 0.f;
     }
-    __syncthreads();
+    if (di) {
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < kGlueRegs; ++i) ss = fmaf(dv[i], dv[i], ss);
+      ss = consumers_sum(ss, red);
+      trace_mark(p.trace, 8);
+      const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, hf), p.eps)));
+#pragma unroll
+      for (int i = 0; i < kGlueRegs; ++i) xv[i] = bf16_round(xv[i] + bf16_round(dv[i] * inv));
+      trace_mark(p.trace, 9);
+    }
     if (blockIdx.x == 0 && p.x_out) {
-      for (uint32_t h = threadIdx.x; h < H; h += blockDim.x)
-        p.x_out[static_cast<size_t>(tok) * H + h] = bf16_bits_rn(xt[h]);
+#pragma unroll
+      for (int i = 0; i < kGlueRegs; ++i) {
+        const uint32_t h = threadIdx.x + i * NTHR;
+        if (h < H) p.x_out[static_cast<size_t>(tok) * H + h] = bf16_bits_rn(xv[i]);
+      }
     }
     float ss = 0.f;
-    for (uint32_t h = threadIdx.x; h < H; h += blockDim.x) ss = fmaf(xt[h], xt[h], ss);
-    ss = block_sum(ss, red);
+#pragma unroll
+    for (int i = 0; i < kGlueRegs; ++i) ss = fmaf(xv[i], xv[i], ss);
+    trace_mark(p.trace, 10);
+    ss = consumers_sum(ss, red);
+    trace_mark(p.trace, 11);
     const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, hf), p.eps)));
-    for (uint32_t h = threadIdx.x; h < H; h += blockDim.x) xt[h] = bf16_round(xt[h] * inv);
-    __syncthreads();
+    float* xt = tmp + static_cast<size_t>(tok) * H;
+#pragma unroll
+    for (int i = 0; i < kGlueRegs; ++i) {
+      const uint32_t h = threadIdx.x + i * NTHR;
+      if (h < H) xt[h] = bf16_round(xv[i] * inv);
+    }
   }
+  consumers_sync();
 }
 
 template <int NT, bool SPLIT, bool FAST>
-__global__ void __launch_bounds__(kWarpsPerCta * 32, 1) ffn_kernel(const FfnParams p) {
+__global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_kernel(const FfnParams p) {
   constexpr int NCA = SPLIT ? 2 * NT : NT;
   constexpr int NCB = NT;
+  constexpr uint32_t NTHR = kConsumerWarps * 32;
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t gw = participant_index(blockIdx.x, warp, gridDim.x);
   const uint64_t Wtot = static_cast<uint64_t>(gridDim.x) * kWarpsPerCta;
   const uint64_t UA = static_cast<uint64_t>(p.gu.RT) * p.gu.KT;
   const uint64_t UB = static_cast<uint64_t>(p.dn.RT) * p.dn.KT;
   const uint64_t WA = effective_warps(Wtot, UA, p.gu.KT), WB = effective_warps(Wtot, UB, p.dn.KT);
+  Shape::init_barriers(smem, p.nst);
+  __syncthreads();
+  const int c = warp < kConsumerWarps ? warp : lane;
+  const uint32_t gw = participant_index(blockIdx.x, static_cast<uint32_t>(c), gridDim.x);
   uint32_t a0 = 0, a1 = 0, b0 = 0, b1 = 0;
-  if (gw < WA) {
+  if (c < kConsumerWarps && gw < WA) {
     a0 = static_cast<uint32_t>(range_start(gw, UA, WA));
     a1 = static_cast<uint32_t>(range_start(gw + 1, UA, WA));
   }
-  if (gw < WB) {
+  if (c < kConsumerWarps && gw < WB) {
     b0 = static_cast<uint32_t>(range_start(gw, UB, WB));
     b1 = static_cast<uint32_t>(range_start(gw + 1, UB, WB));
   }
-  WarpRing<kUnitsPerStage> ring;
-  ring_place(ring, smem, warp, p.nst);
-  ring.status = p.status;
-  ring.setup(p.gu.units + static_cast<size_t>(a0) * kUnitBytes, a1 - a0,
-             p.dn.units + static_cast<size_t>(b0) * kUnitBytes, b1 - b0);
-  ring.init_and_prime(lane);
-
+  // Shared layout after the rings: [xs frags][red][tmp ntok*H f32][x_in raw][down_in raw][xbar]
   uint8_t* xs = smem + ring_smem_bytes(p.nst);
   const size_t xs_bytes_a = frag_bytes(p.gu.KT, NCA);
   const size_t xs_bytes_b = frag_bytes(p.dn.KT, NCB);
   const size_t xs_bytes = xs_bytes_a > xs_bytes_b ? xs_bytes_a : xs_bytes_b;
   float* red = reinterpret_cast<float*>(xs + xs_bytes);
   float* tmp = red + 32;
+  const size_t glue_vals = p.glue ? static_cast<size_t>(p.ntok) * p.H : 0;
+  uint16_t* xraw = reinterpret_cast<uint16_t*>(tmp + glue_vals);
+  float* draw = reinterpret_cast<float*>(xraw + (p.glue_tma ? glue_vals : 0));
+  uint64_t* xbar = reinterpret_cast<uint64_t*>(draw + (p.glue_tma && p.down_in ? glue_vals : 0));
+  const bool tma_in = p.glue && p.glue_tma;
+  if (tma_in && threadIdx.x == 0) {
+    mbar_init(xbar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (warp == kConsumerWarps) {
+    const WorkList wl{p.gu.units + static_cast<size_t>(a0) * kUnitBytes,
+                      p.dn.units + static_cast<size_t>(b0) * kUnitBytes, a1 - a0, b1 - b0};
+    const uint64_t pol = l2_policy_evict_first();
+    if (tma_in) {
+      // The layer inputs go first, ahead of the weight stream.
+      if (lane == 0) {
+        const uint32_t xb = static_cast<uint32_t>(glue_vals * 2), db = p.down_in ? static_cast<uint32_t>(glue_vals * 4) : 0;
+        mbar_arrive_expect_tx(xbar, xb + db);
+        bulk_g2s(xraw, p.x_in, xb, xbar, pol);
+        if (db) bulk_g2s(draw, p.down_in, db, xbar, pol);
+      }
+    } else {
+      producer_wait_release();
+    }
+    produce<kUnitsPerStage>(smem, p.nst, wl, pol, p.status);
+    return;
+  }
+  ConsumerRing<kUnitsPerStage> ring;
+  ring.setup(smem, p.nst, warp, (a1 - a0) + (b1 - b0));
+  trace_mark(p.trace, 0);
 
+  // The act padding (k in [I, 64*dn.KT)) must read as zero in phase B.
+  if (blockIdx.x == 0) {
+    const uint32_t kpad = p.dn.KT * 64;
+    for (uint32_t e = threadIdx.x; e < (kpad - p.I) * NCB; e += NTHR) {
+      const uint32_t n = e % NCB, k = p.I + e / NCB;
+      *reinterpret_cast<uint16_t*>(p.act + frag_offset(NCB, n, k)) = 0;
+    }
+  }
+  bool in_ok = true;
   if (p.glue) {
-    ffn_glue_prologue(p, tmp, red);
+    if (tma_in) in_ok = consumers_and(mbar_wait_bounded(xbar, 0));
+    if (!in_ok && threadIdx.x == 0) atomicOr(p.status, kStatusMbarTimeout);
+    trace_mark(p.trace, 6);
+    ffn_glue_prologue(p, tma_in ? xraw : p.x_in, tma_in ? (p.down_in ? draw : nullptr) : p.down_in, tmp, red);
+    trace_mark(p.trace, 7);
     stage_frags<NCA, false>(xs, p.gu.KT, SmemSrc{tmp, p.ntok, p.H});
   } else {
     stage_frags<NCA, SPLIT>(xs, p.gu.KT, p.x);
   }
-  __syncthreads();
+  consumers_sync();
+  if (!tma_in) consumers_release_producer();
+  trace_mark(p.trace, 1);
 
-  GateUpEpi ge{p.act, p.I, p.act_ld, p.gu.scale_mul, p.fn};
+  GateUpEpi ge{p.act, p.I, NCB, p.gu.scale_mul, p.fn};
   const bool ok = consume_range<NCA, SPLIT, FAST>(ring, p.gu, a0, a1, xs, p.fxA, gw, static_cast<uint32_t>(WA),
                                                   p.ntok, ge, p.status);
+  if (p.trace) {
+    consumers_sync();
+    trace_mark(p.trace, 2);
+  }
   const bool bar_ok = grid_barrier(p.bar, gridDim.x, p.status);
-  if (!bar_ok || !__syncthreads_and(ok)) {
-    if (ok) ring.drain();
+  trace_mark(p.trace, 3);
+  if (!bar_ok || !consumers_and(ok)) {
+    ring.drain(lane);
     return;
   }
-  stage_frags<NCB, false>(xs, p.dn.KT, ActSrc{p.act, p.ntok, p.I, p.act_ld});
-  __syncthreads();
-  consume_range<NCB, false, FAST>(ring, p.dn, b0, b1, xs, p.fxB, gw, static_cast<uint32_t>(WB), p.ntok, p.out,
-                                  p.status);
+  // act is already in fragment order: stage it with 16-byte copies through L2.
+  for (uint32_t o = threadIdx.x * 16; o < xs_bytes_b; o += NTHR * 16)
+    *reinterpret_cast<uint4*>(xs + o) = __ldcg(reinterpret_cast<const uint4*>(p.act + o));
+  consumers_sync();
+  trace_mark(p.trace, 4);
+  if (!consume_range<NCB, false, FAST>(ring, p.dn, b0, b1, xs, p.fxB, gw, static_cast<uint32_t>(WB), p.ntok,
+                                       p.out, p.status))
+    ring.drain(lane);
+  if (p.trace) {
+    consumers_sync();
+    trace_mark(p.trace, 5);
+  }
 }
 
 // Final residual of an FFN stack (single CTA).

@@ -40,6 +40,7 @@ constexpr int kUnitBytes = 576;
 constexpr int kUnitNibBytes = 512;
 constexpr int kTileRows = 16;
 constexpr int kTileCols = 64;
+constexpr int kConsumerWarps = 15;  // + 1 producer warp = 16 warps, 4 per SM sub-partition
 
 struct Q4Mat {
   const uint8_t* units;  // RT*KT units of kUnitBytes
@@ -110,15 +111,17 @@ constexpr uint32_t kNeg8Sub = 0x80088008u;
 // so one lane fetches a unit's fragments with two 128-bit loads.  Column n is
 // token n (bf16 x) or token n/2, hi (n even) / lo (n odd) part (fp32 x).
 // ---------------------------------------------------------------------------
+// Called by the consumer threads (threads [0, NTHR)) only.
 template <int NCOLS, bool SPLIT, class Src>
 __device__ void stage_frags(uint8_t* xs, uint32_t KT, const Src& src) {
   constexpr int BATCH = 8;  // entries per thread per pass: all loads in flight together
+  constexpr uint32_t NTHR = kConsumerWarps * 32;
   const uint32_t total = KT * 4 * NCOLS * 4;
-  for (uint32_t base = 0; base < total; base += blockDim.x * BATCH) {
+  for (uint32_t base = 0; base < total; base += NTHR * BATCH) {
     float v[BATCH][4];
 #pragma unroll
     for (int u = 0; u < BATCH; ++u) {
-      const uint32_t e = base + u * blockDim.x + threadIdx.x;
+      const uint32_t e = base + u * NTHR + threadIdx.x;
       const uint32_t j = e & 3, t4 = (e >> 2) & 3, n = (e >> 4) % NCOLS, kt = (e >> 4) / NCOLS;
       const uint32_t tok = SPLIT ? (n >> 1) : n;
       const uint32_t k0 = kt * 64 + j * 16 + 2 * t4;
@@ -129,7 +132,7 @@ __device__ void stage_frags(uint8_t* xs, uint32_t KT, const Src& src) {
     }
 #pragma unroll
     for (int u = 0; u < BATCH; ++u) {
-      const uint32_t e = base + u * blockDim.x + threadIdx.x;
+      const uint32_t e = base + u * NTHR + threadIdx.x;
       if (e >= total) continue;
       const bool lo = SPLIT && (((e >> 4) % NCOLS) & 1);
       uint16_t h[4];
@@ -152,98 +155,75 @@ __host__ __device__ constexpr size_t frag_bytes(uint32_t KT, int ncols) {
 }
 
 // ---------------------------------------------------------------------------
-// Per-warp ring filled by the TMA engine.  The warp's work list is up to two
-// contiguous unit ranges (segment 0 then segment 1, e.g. FFN gate/up then
-// down); stages hold UPS consecutive list units and may straddle the two
-// segments.  All bookkeeping is incremental 32-bit arithmetic.
+// Warp-specialized unit rings.  Each consumer warp of a CTA owns a ring of
+// nst stages of UPS units; one more warp (the producer) fills them with
+// 1-D bulk copies through the TMA engine.  Per stage: `full` (producer
+// arrive.expect_tx, completed by the copy) and `empty` (consumer lane 0
+// arrives after the stage's data has been read and used).  A consumer's work
+// list is up to two contiguous unit ranges (segment 0 then segment 1, e.g.
+// FFN gate/up then down); a stage may straddle them.
 // ---------------------------------------------------------------------------
+
+// Work list of one consumer warp.
+struct WorkList {
+  const uint8_t* s0;   // first unit of segment 0
+  const uint8_t* s1;   // first unit of segment 1
+  uint32_t c0, c1;     // units in each segment
+};
+
 template <int UPS>
-struct WarpRing {
+struct RingShape {
   static constexpr uint32_t kStageBytes = UPS * kUnitBytes;
-  uint8_t* ring;            // nst * kStageBytes (shared)
-  uint64_t* bars;           // nst mbarriers (shared)
-  uint64_t policy;
-  uint32_t nst;             // number of stages
-  // producer (lane 0 issues; every lane keeps the same counters)
-  const uint8_t* p_src;     // source of the next unit to issue
-  const uint8_t* seg1;      // first unit of segment 1
-  const uint8_t* seg0_end;  // one past the last unit of each segment
-  const uint8_t* seg1_end;
-  uint32_t* status;         // device status word (bounds violations)
-  uint32_t p_left0;         // units of segment 0 not yet issued
-  uint32_t p_left;          // units not yet issued
-  uint32_t p_stage;         // stage the next group goes to
-  // consumer
-  uint32_t stage, phase;    // current stage and its parity
+  // [rings: consumers x nst x stage][full: consumers x nst][empty: consumers x nst]
+  __host__ __device__ static constexpr size_t smem_bytes(uint32_t nst) {
+    return static_cast<size_t>(kConsumerWarps) * nst * (kStageBytes + 16);
+  }
+  __device__ static uint8_t* ring(uint8_t* smem, uint32_t nst, int c) {
+    return smem + static_cast<size_t>(c) * nst * kStageBytes;
+  }
+  __device__ static uint64_t* full(uint8_t* smem, uint32_t nst, int c) {
+    return reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(kConsumerWarps) * nst * kStageBytes) + c * nst;
+  }
+  __device__ static uint64_t* empty(uint8_t* smem, uint32_t nst, int c) {
+    return full(smem, nst, c) + kConsumerWarps * nst;
+  }
+  // All threads: initialize every barrier, then the caller syncs the CTA.
+  __device__ static void init_barriers(uint8_t* smem, uint32_t nst) {
+    uint64_t* f = full(smem, nst, 0);
+    for (uint32_t i = threadIdx.x; i < 2u * kConsumerWarps * nst; i += blockDim.x) mbar_init(&f[i], 1);
+    fence_mbar_init();
+  }
+};
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Consumer side.
+template <int UPS>
+struct ConsumerRing {
+  static constexpr uint32_t kStageBytes = UPS * kUnitBytes;
+  uint32_t ring_saddr;      // shared address of this warp's ring
+  uint64_t* full;
+  uint64_t* empty;
+  uint32_t nst;
+  uint32_t stage, phase;    // current stage and the parity of its next fill
   uint32_t slot;            // units consumed in the current stage
   uint32_t c_left;          // units not yet consumed
 
-  __device__ void setup(const uint8_t* s0, uint32_t c0, const uint8_t* s1, uint32_t c1) {
-    p_src = c0 ? s0 : s1;
-    seg1 = s1;
-    seg0_end = s0 + static_cast<size_t>(c0) * kUnitBytes;
-    seg1_end = s1 + static_cast<size_t>(c1) * kUnitBytes;
-    p_left0 = c0;
-    p_left = c0 + c1;
-    c_left = c0 + c1;
-    p_stage = stage = phase = slot = 0;
+  __device__ void setup(uint8_t* smem, uint32_t nst_, int c, uint32_t total) {
+    nst = nst_;
+    ring_saddr = smem_u32(RingShape<UPS>::ring(smem, nst, c));
+    full = RingShape<UPS>::full(smem, nst, c);
+    empty = RingShape<UPS>::empty(smem, nst, c);
+    stage = phase = slot = 0;
+    c_left = total;
   }
-  // lane 0: copy the next min(UPS, p_left) list units into stage p_stage.
-  // Every copy is checked against the end of its segment; a copy that would
-  // leave it is not issued and reported (the consumer's wait then times out).
-  __device__ __forceinline__ void issue_next() {
-    const uint32_t n = p_left < UPS ? p_left : UPS;
-    uint8_t* dst = ring + p_stage * kStageBytes;
-    uint64_t* bar = &bars[p_stage];
-    if (n <= p_left0 || p_left0 == 0) {
-      const uint8_t* end = p_left0 ? seg0_end : seg1_end;
-      if (p_src + n * kUnitBytes > end) {
-        atomicOr(status, kStatusBadLaunch);
-        return;
-      }
-      mbar_arrive_expect_tx(bar, n * kUnitBytes);
-      bulk_g2s(dst, p_src, n * kUnitBytes, bar, policy);
-    } else {  // the group straddles the end of segment 0
-      if (p_src + p_left0 * kUnitBytes > seg0_end || seg1 + (n - p_left0) * kUnitBytes > seg1_end) {
-        atomicOr(status, kStatusBadLaunch);
-        return;
-      }
-      mbar_arrive_expect_tx(bar, n * kUnitBytes);
-      bulk_g2s(dst, p_src, p_left0 * kUnitBytes, bar, policy);
-      bulk_g2s(dst + p_left0 * kUnitBytes, seg1, (n - p_left0) * kUnitBytes, bar, policy);
-    }
+  __device__ __forceinline__ bool wait_full() {  // warp-uniform result
+    return __all_sync(0xffffffffu, mbar_wait_bounded(&full[stage], phase)) != 0;
   }
-  // every lane: advance the producer counters past one issued group
-  __device__ __forceinline__ void advance_producer() {
-    const uint32_t n = p_left < UPS ? p_left : UPS;
-    if (n < p_left0) {          // still inside segment 0
-      p_src += n * kUnitBytes;
-      p_left0 -= n;
-    } else if (p_left0 > 0) {   // reached or crossed the end of segment 0
-      p_src = seg1 + (n - p_left0) * kUnitBytes;
-      p_left0 = 0;
-    } else {                    // inside segment 1
-      p_src += n * kUnitBytes;
-    }
-    p_left -= n;
-    if (++p_stage == nst) p_stage = 0;
-  }
-  __device__ void init_and_prime(int lane) {
-    if (lane == 0) {
-      for (uint32_t s = 0; s < nst; ++s) mbar_init(&bars[s], 1);
-      fence_mbar_init();
-    }
-    for (uint32_t s = 0; s < nst && p_left; ++s) {
-      if (lane == 0) issue_next();
-      advance_producer();
-    }
-    __syncwarp();
-  }
-  __device__ __forceinline__ bool wait_stage() {  // warp-uniform result
-    return __all_sync(0xffffffffu, mbar_wait_bounded(&bars[stage], phase)) != 0;
-  }
-  __device__ __forceinline__ const uint8_t* unit_ptr() const {
-    return ring + stage * kStageBytes + slot * kUnitBytes;
+  __device__ __forceinline__ uint32_t unit_saddr() const {
+    return ring_saddr + stage * kStageBytes + slot * kUnitBytes;
   }
   // Units left in the current stage (its group holds min(UPS, units left at
   // the group's start) units).
@@ -251,18 +231,15 @@ struct WarpRing {
     const uint32_t at_start = c_left + slot;
     return (at_start < UPS ? at_start : UPS) - slot;
   }
-  // Consume `n` units of the current stage; refill the stage once finished.
-  // The refill overwrites data this warp already read into registers and used,
-  // so no proxy fence is needed (only generic-proxy writes need one).
+  // Consume n units of the current stage; hand a finished stage back.  The
+  // stage's data has been read into registers and used, so the producer may
+  // overwrite it (reads need no proxy fence).
   __device__ __forceinline__ void consume(uint32_t n, int lane) {
     c_left -= n;
     slot += n;
     if (slot == UPS || c_left == 0) {
       __syncwarp();
-      if (p_left) {
-        if (lane == 0) issue_next();
-        advance_producer();
-      }
+      if (lane == 0) mbar_arrive(&empty[stage]);
       slot = 0;
       if (++stage == nst) {
         stage = 0;
@@ -270,21 +247,116 @@ struct WarpRing {
       }
     }
   }
-  // After an error: wait (bounded) for every stage that was issued and not
-  // yet consumed, starting with the current one.
-  __device__ void drain() {
-    const uint32_t issued_not_consumed_units = c_left + slot - p_left;
-    uint32_t groups = (issued_not_consumed_units + UPS - 1) / UPS;
-    uint32_t s = stage, ph = phase;
-    for (; groups; --groups) {
-      (void)mbar_wait_bounded(&bars[s], ph);
-      if (++s == nst) {
-        s = 0;
-        ph ^= 1;
-      }
+  // Error path: keep the protocol moving without computing, so the producer
+  // can finish and no copy is left in flight; stop if a copy never lands.
+  __device__ void drain(int lane) {
+    while (c_left) {
+      if (slot == 0 && !wait_full()) return;
+      consume(stage_left(), lane);
     }
   }
 };
+
+// Producer warp: lane c < kConsumerWarps feeds consumer warp c.  Non-blocking round
+// robin: a lane issues its next group when the target stage is empty; the
+// warp sleeps briefly when no lane made progress.  A lane that sees no
+// progress for kWaitTimeoutNs records a timeout and stops.
+template <int UPS>
+__device__ void produce(uint8_t* smem, uint32_t nst, const WorkList& wl, uint64_t policy, uint32_t* status) {
+  constexpr uint32_t kStageBytes = UPS * kUnitBytes;
+  const int lane = threadIdx.x & 31;
+  const bool mine = lane < kConsumerWarps;
+  uint8_t* ring = mine ? RingShape<UPS>::ring(smem, nst, lane) : nullptr;
+  uint64_t* full = mine ? RingShape<UPS>::full(smem, nst, lane) : nullptr;
+  uint64_t* empty = mine ? RingShape<UPS>::empty(smem, nst, lane) : nullptr;
+  const uint8_t* seg0_end = wl.s0 + static_cast<size_t>(wl.c0) * kUnitBytes;
+  const uint8_t* seg1_end = wl.s1 + static_cast<size_t>(wl.c1) * kUnitBytes;
+  const uint8_t* src = wl.c0 ? wl.s0 : wl.s1;
+  uint32_t left0 = wl.c0;
+  uint32_t left = mine ? wl.c0 + wl.c1 : 0;
+  uint32_t g = 0, pstage = 0, round = 0;  // group, its stage, and g / nst
+  unsigned long long last = globaltimer_ns();
+  while (__any_sync(0xffffffffu, left != 0)) {
+    bool progress = false;
+    if (left) {
+      const bool ready = round == 0 || mbar_try_wait(&empty[pstage], (round - 1) & 1);
+      if (ready) {
+        const uint32_t n = left < UPS ? left : UPS;
+        uint8_t* dst = ring + pstage * kStageBytes;
+        bool ok;
+        if (n <= left0 || left0 == 0) {
+          ok = src + static_cast<size_t>(n) * kUnitBytes <= (left0 ? seg0_end : seg1_end);
+          if (ok) {
+            mbar_arrive_expect_tx(&full[pstage], n * kUnitBytes);
+            bulk_g2s(dst, src, n * kUnitBytes, &full[pstage], policy);
+          }
+        } else {  // the group straddles the end of segment 0
+          ok = src + static_cast<size_t>(left0) * kUnitBytes <= seg0_end &&
+               wl.s1 + static_cast<size_t>(n - left0) * kUnitBytes <= seg1_end;
+          if (ok) {
+            mbar_arrive_expect_tx(&full[pstage], n * kUnitBytes);
+            bulk_g2s(dst, src, left0 * kUnitBytes, &full[pstage], policy);
+            bulk_g2s(dst + left0 * kUnitBytes, wl.s1, (n - left0) * kUnitBytes, &full[pstage], policy);
+          }
+        }
+        if (!ok) {  // a copy would leave its segment: report, stop this lane
+          atomicOr(status, kStatusBadLaunch);
+          left = 0;
+        } else {
+          if (n < left0) {
+            src += static_cast<size_t>(n) * kUnitBytes;
+            left0 -= n;
+          } else if (left0 > 0) {
+            src = wl.s1 + static_cast<size_t>(n - left0) * kUnitBytes;
+            left0 = 0;
+          } else {
+            src += static_cast<size_t>(n) * kUnitBytes;
+          }
+          left -= n;
+          ++g;
+          if (++pstage == nst) {
+            pstage = 0;
+            ++round;
+          }
+          progress = true;
+          last = globaltimer_ns();
+        }
+      } else if (globaltimer_ns() - last > kWaitTimeoutNs) {
+        atomicOr(status, kStatusMbarTimeout);
+        left = 0;
+      }
+    }
+    if (!__any_sync(0xffffffffu, progress)) __nanosleep(128);
+  }
+}
+
+// Barrier 2 (all 16 warps): the producer waits there until the consumers have
+// staged their activations, so those few latency-critical loads are not
+// queued behind the weight stream.
+__device__ __forceinline__ void producer_wait_release() {
+  asm volatile("bar.sync 2, %0;" ::"n"((kConsumerWarps + 1) * 32) : "memory");
+}
+__device__ __forceinline__ void consumers_release_producer() {
+  asm volatile("bar.arrive 2, %0;" ::"n"((kConsumerWarps + 1) * 32) : "memory");
+}
+
+// Named barrier and AND-reduction over the consumer warps only (the producer
+// warp runs free).
+__device__ __forceinline__ void consumers_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+}
+__device__ __forceinline__ bool consumers_and(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "n"(kConsumerWarps * 32)
+      : "memory");
+  return r != 0;
+}
 
 // ---------------------------------------------------------------------------
 // Accumulate one unit.  acc[grp][parity][4] holds the C fragments for column
@@ -294,20 +366,11 @@ struct WarpRing {
 template <int NCOLS, bool FAST>
 struct UnitMath {
   static constexpr int NGRP = NCOLS > 8 ? 2 : 1;
+  static constexpr int kXStride = NCOLS * 128;  // fragment bytes per k tile
 
-  // xl: this lane's fragment base, xs + (n*4 + t4)*32 with n its B column.
-  __device__ __forceinline__ static void run(const uint8_t* ubuf, const uint8_t* xl, uint32_t kt, int lane,
-                                             float (&acc)[NGRP][2][4]) {
-    const int g = lane >> 2;
-    const uint4 nib = lds128(ubuf + lane * 16);
-    const uint2 sc = lds64(ubuf + kUnitNibBytes + g * 8);
-    uint4 xf[NGRP][2];
-#pragma unroll
-    for (int grp = 0; grp < NGRP; ++grp) {
-      const uint8_t* xk = xl + static_cast<size_t>(kt) * (NCOLS * 128) + grp * (8 * 128);
-      xf[grp][0] = lds128(xk);
-      xf[grp][1] = lds128(xk + 16);
-    }
+  // Core: nibble word, scale pair and fragments already in registers.
+  __device__ __forceinline__ static void math(const uint4& nib, const uint2& sc, const uint4 (&xf)[NGRP][2],
+                                              float (&acc)[NGRP][2][4]) {
     uint32_t S[2][2], C[2][2];  // [block][row g / row g+8]
     S[0][0] = bf2_bcast(sc.x, 0);
     S[1][0] = bf2_bcast(sc.x, 1);
@@ -332,6 +395,44 @@ struct UnitMath {
       }
     }
   }
+
+  // Unit S of a stage: nib_base = stage + lane*16, sc_base = stage + 512 + g*8,
+  // x_base = this lane's fragments of the stage's first k tile.
+  template <int S>
+  __device__ __forceinline__ static void at(uint32_t nib_base, uint32_t sc_base, uint32_t x_base,
+                                            float (&acc)[NGRP][2][4]) {
+    const uint4 nib = lds128_at<S * kUnitBytes>(nib_base);
+    const uint2 sc = lds64_at<S * kUnitBytes>(sc_base);
+    uint4 xf[NGRP][2];
+    xf[0][0] = lds128_at<S * kXStride>(x_base);
+    xf[0][1] = lds128_at<S * kXStride + 16>(x_base);
+    if constexpr (NGRP > 1) {
+      xf[NGRP - 1][0] = lds128_at<S * kXStride + 1024>(x_base);
+      xf[NGRP - 1][1] = lds128_at<S * kXStride + 1024 + 16>(x_base);
+    }
+    math(nib, sc, xf, acc);
+  }
+
+  // Generic form (runtime unit address and k tile; shared-space addresses).
+  __device__ __forceinline__ static void run_saddr(uint32_t u, uint32_t x_saddr, uint32_t kt, int lane,
+                                                   float (&acc)[NGRP][2][4]) {
+    const int g = lane >> 2;
+    at<0>(u + lane * 16, u + kUnitNibBytes + g * 8, x_saddr + kt * kXStride, acc);
+  }
+};
+
+// Straight-line run of units S..UPS-1 of a full stage.
+template <int NCOLS, bool FAST, int S, int UPS>
+struct StageUnroll {
+  __device__ __forceinline__ static void go(uint32_t nib_base, uint32_t sc_base, uint32_t x_base,
+                                            float (&acc)[NCOLS > 8 ? 2 : 1][2][4]) {
+    UnitMath<NCOLS, FAST>::template at<S>(nib_base, sc_base, x_base, acc);
+    StageUnroll<NCOLS, FAST, S + 1, UPS>::go(nib_base, sc_base, x_base, acc);
+  }
+};
+template <int NCOLS, bool FAST, int UPS>
+struct StageUnroll<NCOLS, FAST, UPS, UPS> {
+  __device__ __forceinline__ static void go(uint32_t, uint32_t, uint32_t, float (&)[NCOLS > 8 ? 2 : 1][2][4]) {}
 };
 
 // ---------------------------------------------------------------------------
@@ -421,7 +522,7 @@ __device__ __forceinline__ void flush_tile(const float (&acc)[(NCOLS > 8 ? 2 : 1
   if (old != w_hi - w_lo) return;
   // Gather the contributors' partials CB at a time (independent loads in
   // flight), then add them in warp order.
-  constexpr int CB = 8 / LV::T;
+  constexpr int CB = 16 / LV::T;
   float sg[LV::T], sg8[LV::T];
 #pragma unroll
   for (int i = 0; i < LV::T; ++i) sg[i] = sg8[i] = 0.f;
@@ -465,7 +566,7 @@ __device__ __forceinline__ void flush_tile(const float (&acc)[(NCOLS > 8 ? 2 : 1
 // draining the ring).  W = participating warps for this matrix.
 // ---------------------------------------------------------------------------
 template <int NCOLS, bool SPLIT, bool FAST, int UPS, class Epi>
-__device__ bool consume_range(WarpRing<UPS>& ring, const Q4Mat& m, uint32_t u0, uint32_t u1,
+__device__ bool consume_range(ConsumerRing<UPS>& ring, const Q4Mat& m, uint32_t u0, uint32_t u1,
                               const uint8_t* xs, const Fixup& fx, uint32_t gw, uint32_t W, int ntok,
                               const Epi& epi, uint32_t* status) {
   constexpr int NGRP = NCOLS > 8 ? 2 : 1;
@@ -475,6 +576,7 @@ __device__ bool consume_range(WarpRing<UPS>& ring, const Q4Mat& m, uint32_t u0, 
   const uint64_t U = static_cast<uint64_t>(m.RT) * KT;
   const uint32_t n_lane = NCOLS >= 8 ? g : (g & (NCOLS - 1));
   const uint8_t* xl = xs + (n_lane * 4 + t4) * 32;
+  const uint32_t x_saddr = smem_u32(xl);
   const uint32_t first_row = u0 / KT;
   uint32_t r = first_row;
   uint32_t kt = u0 - r * KT;
@@ -488,19 +590,19 @@ __device__ bool consume_range(WarpRing<UPS>& ring, const Q4Mat& m, uint32_t u0, 
 #pragma unroll
       for (int c = 0; c < 4; ++c) acc[a][b][c] = 0.f;
   while (left) {
-    if (ring.slot == 0 && !ring.wait_stage()) {
+    if (ring.slot == 0 && !ring.wait_full()) {
       if (lane == 0) atomicOr(status, kStatusMbarTimeout);
-      ring.drain();
       return false;
     }
     const uint32_t sl = ring.stage_left();
     const uint32_t take = sl < left ? sl : left;
-    const uint8_t* sp = ring.unit_ptr();
+    const uint32_t su = ring.unit_saddr();
     if (take == UPS && kt + UPS < KT) {
       // Common case: a full stage inside one row tile -- straight-line code so
-      // the UPS units' dequant and MMA chains interleave.
-#pragma unroll
-      for (int s = 0; s < UPS; ++s) UnitMath<NCOLS, FAST>::run(sp + s * kUnitBytes, xl, kt + s, lane, acc);
+      // the UPS units' dequant and MMA chains interleave; all shared-memory
+      // offsets are immediates.
+      StageUnroll<NCOLS, FAST, 0, UPS>::go(su + lane * 16, su + kUnitNibBytes + g * 8,
+                                           x_saddr + kt * UnitMath<NCOLS, FAST>::kXStride, acc);
       kt += UPS;
       ring.consume(take, lane);
       left -= take;
@@ -509,7 +611,7 @@ __device__ bool consume_range(WarpRing<UPS>& ring, const Q4Mat& m, uint32_t u0, 
 #pragma unroll
     for (int s = 0; s < UPS; ++s) {
       if (static_cast<uint32_t>(s) < take) {
-        UnitMath<NCOLS, FAST>::run(sp + s * kUnitBytes, xl, kt, lane, acc);
+        UnitMath<NCOLS, FAST>::run_saddr(su + s * kUnitBytes, x_saddr, kt, lane, acc);
         if (++kt == KT) {
           flush_tile<NCOLS, SPLIT>(acc, seg_kt0 == 0, r, first_row, KT, U, W, fx, gw, ntok, epi);
 #pragma unroll

@@ -22,6 +22,19 @@ from . import _lib
 from .ops import FusedFFNWeight
 
 
+def tp_slice(I: int, rank: int, world: int) -> tuple[int, int]:
+    """Intermediate-dimension slice [begin, end) of `rank` in a `world`-way
+    tensor-parallel FFN: contiguous, 32-aligned (whole Q4 blocks of the down
+    projection's rows), as the reference splits I over AIE cores
+    (kernels/ffn_fused/ffn_fused.py:59-60)."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("bad rank/world")
+    if I % (32 * world):
+        raise ValueError(f"I={I} does not split into {world} slices of whole 32-blocks")
+    step = I // world
+    return rank * step, (rank + 1) * step
+
+
 class FFNStack:
     """Resident FFN stack on one GPU (one rank of a tensor-parallel group).
 
@@ -33,12 +46,9 @@ class FFNStack:
 
     def __init__(self, H: int, I: int, device: int = 0, rank: int = 0, world: int = 1,
                  activation: str = "gelu"):
-        if I % (32 * world):
-            raise ValueError("I must split into 32-aligned slices over the ranks")
         self.H, self.I, self.device, self.rank, self.world = H, I, device, rank, world
         self.activation = activation
-        self.i_begin = rank * I // world
-        self.i_end = (rank + 1) * I // world
+        self.i_begin, self.i_end = tp_slice(I, rank, world)
         self.layers: list[FusedFFNWeight] = []
         dev = torch.device("cuda", device)
         self.x = [torch.zeros(H, dtype=torch.bfloat16, device=dev) for _ in range(2)]

@@ -243,13 +243,15 @@ def run_ours(args) -> None:
     for _ in range(args.warmup):
         stack.replay()
     s.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
+    # start the clock sampler before the barrier: no rank may be held up
+    # inside the timed region by another rank's host-side work
     clocks = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
     if clocks:
         clocks.start()
         time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(s):
         e0.record(s)

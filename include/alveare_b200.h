@@ -160,6 +160,16 @@ int alv_ffn_stack_finalize(alv_ctx* ctx, int ntok, int H, const uint16_t* x_in,
 int alv_gemv_noalloc(alv_ctx* ctx, alv_handle h, int ntok, const void* x, int x_dtype, void* y,
                      int y_dtype, void* stream);
 
+/* Tracing (the reference's per-launch timers, npu.cpp:23-43): when `trace`
+ * is a device buffer of (#SMs x 16) uint64, every later alv_ffn / alv_ffn_layer
+ * launch writes per-CTA %globaltimer stamps (ns): [0] start, [1] input staged,
+ * [2] gate/up phase done, [3] grid barrier passed, [4] act staged, [5] down
+ * phase done; with the layer glue also [6] inputs landed, [7] glue done,
+ * [8]/[9] post-norm reduction / residual done, [10]/[11] pre-norm reduction
+ * entered / left.  Slots [12]-[15] are unused.  NULL turns tracing off (the
+ * default). */
+int alv_set_trace(alv_ctx* ctx, uint64_t* trace);
+
 /* ---- host-buffer convenience (synchronous, like NpuRegistry::run_gemv) ---- */
 
 /* Copy x from host memory, run, copy y back to host memory, synchronize and
