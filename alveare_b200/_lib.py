@@ -50,6 +50,8 @@ SIGNATURES = {
     "alv_ffn": (_i, [_vp, _u32, _i, _vp, _i, _vp, _i, _vp]),
     "alv_ffn_layer": (_i, [_vp, _u32, _i, _vp, _vp, _vp, _vp, _vp]),
     "alv_ffn_stack_finalize": (_i, [_vp, _i, _i, _vp, _vp, _vp, _vp]),
+    "alv_ffn_stack_create": (_i, [_vp, _c.POINTER(_u32), _i, _c.POINTER(_u32)]),
+    "alv_ffn_stack_run": (_i, [_vp, _u32, _i, _vp, _vp, _vp]),
     "alv_run_gemv": (_i, [_vp, _u32, _i, _vp, _i, _vp, _i]),
     "alv_run_ffn": (_i, [_vp, _u32, _i, _vp, _i, _vp, _i]),
     "alv_gemv_noalloc": (_i, [_vp, _u32, _i, _vp, _i, _vp, _i, _vp]),

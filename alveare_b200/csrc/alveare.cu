@@ -5,9 +5,11 @@
 #include <algorithm>
 #include <climits>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <mutex>
+#include <map>
 #include <set>
 #include <string>
 #include <vector>
@@ -32,10 +34,16 @@ struct Mat {
 };
 
 struct Weight {
-  int kind = 0;  // 1 gemv, 2 ffn
-  Mat a, b;      // gemv: a; ffn: a = gate/up interleaved, b = down
+  int kind = 0;  // 1 gemv, 2 ffn, 3 ffn stack
+  Mat a, b;      // gemv: a; ffn: a = gate/up interleaved, b = down; stack: shapes of every layer
   uint32_t H = 0, I = 0, i_begin = 0, i_end = 0;
   int act = 0;
+  // kind 3: the layers (FFN weights), their device descriptors and the
+  // stack's own workspace (sync words, split-K partials, down, act)
+  std::vector<alv_handle> layers;
+  LayerW* layers_dev = nullptr;
+  uint8_t* ws = nullptr;
+  size_t ws_bytes = 0;
 };
 
 }  // namespace
@@ -45,8 +53,10 @@ struct alv_ctx {
   int num_sms = 0;
   std::string err;
   std::vector<std::unique_ptr<Weight>> weights;  // handle = index + 1
-  uint8_t* scratch = nullptr;                    // [header][counters][work]
+  uint8_t* sync = nullptr;                       // [header: status, grid barrier][counters], fixed
+  uint8_t* scratch = nullptr;                    // work area (split-K partials, act)
   size_t scratch_bytes = 0;
+  std::vector<void*> retired;                    // outgrown buffers, freed with the context
   void* io = nullptr;                            // device staging for host-buffer calls
   size_t io_bytes = 0;
   cudaStream_t stream = nullptr;                 // internal stream (loads, host calls)
@@ -72,23 +82,27 @@ int set_device(alv_ctx* ctx) {
   return ALV_OK;
 }
 
-uint32_t* status_ptr(alv_ctx* ctx) { return reinterpret_cast<uint32_t*>(ctx->scratch); }
-GridBar* bar_ptr(alv_ctx* ctx) { return reinterpret_cast<GridBar*>(ctx->scratch + 256); }
-uint32_t* counters_ptr(alv_ctx* ctx) { return reinterpret_cast<uint32_t*>(ctx->scratch + kHeaderBytes); }
-uint8_t* work_ptr(alv_ctx* ctx) {
-  return ctx->scratch + kHeaderBytes + static_cast<size_t>(kMaxCounters) * 4;
-}
+constexpr size_t kSyncBytes = kHeaderBytes + static_cast<size_t>(kMaxCounters) * 4;
+uint32_t* status_ptr(alv_ctx* ctx) { return reinterpret_cast<uint32_t*>(ctx->sync); }
+GridBar* bar_ptr(alv_ctx* ctx) { return reinterpret_cast<GridBar*>(ctx->sync + 256); }
+uint32_t* counters_ptr(alv_ctx* ctx) { return reinterpret_cast<uint32_t*>(ctx->sync + kHeaderBytes); }
+uint8_t* work_ptr(alv_ctx* ctx) { return ctx->scratch; }
 
-// The scratch arena: header and counters keep their offsets forever (counters
-// are only ever counters and are zero between launches); the work area above
-// them is re-laid out per call.
+// The sync block (status word, grid barrier, arrival counters; counters are
+// zero between launches) is allocated once per context.  The work area is
+// re-laid out per call and grows on demand; an outgrown area is kept until
+// the context is destroyed, so launches captured in a CUDA graph earlier
+// still point at live memory.
 int ensure_scratch(alv_ctx* ctx, size_t work_bytes) {
-  const size_t need = kHeaderBytes + static_cast<size_t>(kMaxCounters) * 4 + work_bytes;
-  if (ctx->scratch && ctx->scratch_bytes >= need) return ALV_OK;
+  if (!ctx->sync) {
+    ALV_CUDA(ctx, cudaMalloc(&ctx->sync, kSyncBytes));
+    ALV_CUDA(ctx, cudaMemset(ctx->sync, 0, kSyncBytes));
+  }
+  if (ctx->scratch && ctx->scratch_bytes >= work_bytes) return ALV_OK;
   ALV_CUDA(ctx, cudaDeviceSynchronize());
-  if (ctx->scratch) ALV_CUDA(ctx, cudaFree(ctx->scratch));
+  if (ctx->scratch) ctx->retired.push_back(ctx->scratch);
   ctx->scratch = nullptr;
-  const size_t bytes = std::max(need, static_cast<size_t>(8) << 20);
+  const size_t bytes = std::max(work_bytes, static_cast<size_t>(8) << 20);
   ALV_CUDA(ctx, cudaMalloc(&ctx->scratch, bytes));
   ALV_CUDA(ctx, cudaMemset(ctx->scratch, 0, bytes));
   ctx->scratch_bytes = bytes;
@@ -198,36 +212,45 @@ int stage_source(alv_ctx* ctx, const void* src, size_t bytes, int on_device, con
 // ---------------------------------------------------------------------------
 // Raise the kernel's dynamic shared-memory limit once per (kernel, device) to
 // the maximum, so launches need no per-call attribute changes.
+// (The limit covers static + dynamic shared memory; kernels with static
+// __shared__ arrays get kMaxSmem minus those bytes.)
 template <class K>
 int prepare_kernel(alv_ctx* ctx, K kernel, size_t smem) {
-  if (smem > kMaxSmem)
-    return fail(ctx, ALV_ERR_UNSUPPORTED, "problem needs " + std::to_string(smem) +
-                                              " B of shared memory (max " + std::to_string(kMaxSmem) + ")");
   static std::mutex mu;
-  static std::set<std::pair<const void*, int>> done;
+  static std::map<std::pair<const void*, int>, size_t> max_dyn;
   const auto key = std::make_pair(reinterpret_cast<const void*>(kernel), ctx->device);
   std::lock_guard<std::mutex> lock(mu);
-  if (!done.count(key)) {
-    ALV_CUDA(ctx, cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(kMaxSmem)));
-    done.insert(key);
+  auto it = max_dyn.find(key);
+  if (it == max_dyn.end()) {
+    cudaFuncAttributes fa;
+    ALV_CUDA(ctx, cudaFuncGetAttributes(&fa, kernel));
+    const size_t dyn = fa.sharedSizeBytes < kMaxSmem ? kMaxSmem - fa.sharedSizeBytes : 0;
+    ALV_CUDA(ctx, cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(dyn)));
+    it = max_dyn.emplace(key, dyn).first;
   }
+  if (smem > it->second)
+    return fail(ctx, ALV_ERR_UNSUPPORTED, "problem needs " + std::to_string(smem) +
+                                              " B of dynamic shared memory (max " + std::to_string(it->second) + ")");
   return ALV_OK;
 }
 
-// Ring stages per warp that fit beside `other` bytes of shared memory (max 3).
+// Ring stages per warp that fit beside `other` bytes of dynamic shared memory
+// (at most kMaxStages), leaving room for the kernels' static shared memory
+// (per-warp work lists and copy cursors, < kStaticSmemReserve bytes).
+constexpr size_t kStaticSmemReserve = 2048;
+constexpr uint32_t kMaxStages = 24 / kUnitsPerStage;
 uint32_t ring_stages(size_t other) {
-  for (uint32_t nst = 3; nst >= 1; --nst)
-    if (ring_smem_bytes(nst) + other <= kMaxSmem) return nst;
+  for (uint32_t nst = kMaxStages; nst >= 1; --nst)
+    if (ring_smem_bytes(nst) + other + kStaticSmemReserve <= kMaxSmem) return nst;
   return 0;
 }
 
 template <int NCOLS, bool SPLIT, bool FAST>
 int launch_gemv_t(alv_ctx* ctx, GemvParams p, cudaStream_t st) {
-  const size_t xs = frag_bytes(p.m.KT, NCOLS);
-  p.nst = ring_stages(xs);
+  const size_t other = part_bytes(p.x.ntok) + frag_bytes(p.m.KT, NCOLS);
+  p.nst = ring_stages(other);
   if (!p.nst) return fail(ctx, ALV_ERR_UNSUPPORTED, "gemv: K too large for the shared-memory fragment stage");
-  const size_t smem = ring_smem_bytes(p.nst) + xs;
+  const size_t smem = ring_smem_bytes(p.nst) + other;
   auto k = gemv_kernel<NCOLS, SPLIT, FAST>;
   int rc = prepare_kernel(ctx, k, smem);
   if (rc) return rc;
@@ -264,7 +287,7 @@ int launch_gemv(alv_ctx* ctx, const GemvParams& p, bool split, uint32_t ncols, c
 template <int NT, bool SPLIT, bool FAST>
 int launch_ffn_t(alv_ctx* ctx, FfnParams p, cudaStream_t st) {
   constexpr int NCA = SPLIT ? 2 * NT : NT;
-  size_t other = std::max(frag_bytes(p.gu.KT, NCA), frag_bytes(p.dn.KT, NT)) + 32 * sizeof(float);
+  size_t other = part_bytes(p.ntok) + std::max(frag_bytes(p.gu.KT, NCA), frag_bytes(p.dn.KT, NT)) + 32 * sizeof(float);
   if (p.glue) {
     const size_t v = static_cast<size_t>(p.ntok) * p.H;
     other += v * sizeof(float);                                  // tmp
@@ -307,10 +330,9 @@ int launch_ffn(alv_ctx* ctx, const FfnParams& p, bool split, uint32_t nt, cudaSt
   return p.gu.fast ? launch_ffn_f<true>(ctx, p, split, nt, st) : launch_ffn_f<false>(ctx, p, split, nt, st);
 }
 
-size_t ws_floats(alv_ctx* ctx, const Q4Mat& m, int ntok) {
-  const uint64_t U = static_cast<uint64_t>(m.RT) * m.KT;
-  const uint64_t W = effective_warps(static_cast<uint64_t>(ctx->num_sms) * kWarpsPerCta, U, m.KT);
-  return static_cast<size_t>(W) * 2 * ntok * 16;
+// Split-K CTA partials: two slots of ntok x 16 floats per CTA.
+size_t ws_floats(alv_ctx* ctx, const Q4Mat&, int ntok) {
+  return static_cast<size_t>(ctx->num_sms) * 2 * ntok * 16;
 }
 
 bool valid_dtype(int d) { return d == ALV_F32 || d == ALV_BF16; }
@@ -387,21 +409,34 @@ int do_ffn(alv_ctx* ctx, Weight* w, int ntok, const FfnIo& io, cudaStream_t st) 
 
 int io_buffers(alv_ctx* ctx, size_t bytes) {
   if (ctx->io && ctx->io_bytes >= bytes) return ALV_OK;
-  if (ctx->io) ALV_CUDA(ctx, cudaFree(ctx->io));
+  if (ctx->io) ctx->retired.push_back(ctx->io);
   ctx->io = nullptr;
   ALV_CUDA(ctx, cudaMalloc(&ctx->io, bytes));
   ctx->io_bytes = bytes;
   return ALV_OK;
 }
 
+// Sync block of an FFN stack's workspace: [status @0][GridBar @256][counters @1024].
+size_t stack_sync_bytes(const Weight* w) {
+  return kHeaderBytes + static_cast<size_t>(w->a.m.RT + w->b.m.RT) * 4;
+}
+
 int check_status(alv_ctx* ctx, cudaStream_t st) {
   ALV_CUDA(ctx, cudaStreamSynchronize(st));
-  if (!ctx->scratch) return ALV_OK;
+  if (!ctx->sync) return ALV_OK;
   uint32_t s = 0;
   ALV_CUDA(ctx, cudaMemcpy(&s, status_ptr(ctx), sizeof(s), cudaMemcpyDeviceToHost));
+  // A kernel that gave up mid-way leaves its status word set: clear that
+  // launch's status, barrier and counters.
+  if (s) ALV_CUDA(ctx, cudaMemset(ctx->sync, 0, kSyncBytes));
+  for (auto& w : ctx->weights) {
+    if (!w || w->kind != 3) continue;
+    uint32_t t = 0;
+    ALV_CUDA(ctx, cudaMemcpy(&t, w->ws, sizeof(t), cudaMemcpyDeviceToHost));
+    if (t) ALV_CUDA(ctx, cudaMemset(w->ws, 0, stack_sync_bytes(w.get())));
+    s |= t;
+  }
   if (s) {
-    // A kernel gave up mid-way: clear status, barrier and counters.
-    ALV_CUDA(ctx, cudaMemset(ctx->scratch, 0, kHeaderBytes + static_cast<size_t>(kMaxCounters) * 4));
     char buf[128];
     std::snprintf(buf, sizeof(buf), "device-side wait timed out (status 0x%x)", s);
     return fail(ctx, ALV_ERR_TIMEOUT, buf);
@@ -451,9 +486,13 @@ int alv_ctx_destroy(alv_ctx* ctx) {
     if (!w) continue;
     cudaFree(w->a.dev);
     cudaFree(w->b.dev);
+    cudaFree(w->layers_dev);
+    cudaFree(w->ws);
   }
+  cudaFree(ctx->sync);
   cudaFree(ctx->scratch);
   cudaFree(ctx->io);
+  for (void* q : ctx->retired) cudaFree(q);
   cudaStreamDestroy(ctx->stream);
   delete ctx;
   return ALV_OK;
@@ -594,9 +633,14 @@ int alv_weight_destroy(alv_ctx* ctx, alv_handle h) {
   if (!w) return fail(ctx, ALV_ERR_HANDLE, "weight_destroy: invalid handle");
   int rc = set_device(ctx);
   if (rc) return rc;
+  for (auto& o : ctx->weights)
+    if (o && o->kind == 3 && std::find(o->layers.begin(), o->layers.end(), h) != o->layers.end())
+      return fail(ctx, ALV_ERR_ARG, "weight_destroy: the weight is a layer of an FFN stack; destroy the stack first");
   ALV_CUDA(ctx, cudaDeviceSynchronize());
   cudaFree(w->a.dev);
   cudaFree(w->b.dev);
+  cudaFree(w->layers_dev);
+  cudaFree(w->ws);
   ctx->weights[h - 1].reset();
   return ALV_OK;
 }
@@ -725,9 +769,12 @@ int alv_ffn_stack_finalize(alv_ctx* ctx, int ntok, int H, const uint16_t* x_in, 
                            uint16_t* x_out, void* stream) {
   if (!ctx || !x_in || !down_in || !x_out || ntok < 1 || H <= 0)
     return fail(ctx, ALV_ERR_ARG, "ffn_stack_finalize: bad argument");
+  if (static_cast<uint32_t>(H) > 32u * kConsumerWarps * kGlueRegs)
+    return fail(ctx, ALV_ERR_UNSUPPORTED,
+                "ffn_stack_finalize: H must be <= " + std::to_string(32u * kConsumerWarps * kGlueRegs));
   int rc = set_device(ctx);
   if (rc) return rc;
-  ffn_stack_finalize_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(
+  ffn_stack_finalize_kernel<<<1, kConsumerWarps * 32, 0, static_cast<cudaStream_t>(stream)>>>(
       ntok, static_cast<uint32_t>(H), x_in, down_in, x_out, 1e-6f);
   ALV_CUDA(ctx, cudaGetLastError());
   return ALV_OK;
@@ -776,6 +823,140 @@ int alv_run_ffn(alv_ctx* ctx, alv_handle h, int ntok, const void* x_host, int x_
 }
 
 }  // extern "C"
+
+// ===========================================================================
+// FFN stack: every layer of a decode step in one persistent launch
+// (ffn_stack_kernel).  The stack keeps its own workspace, so a launch
+// captured in a CUDA graph stays valid whatever else the context runs.
+// ===========================================================================
+namespace {
+constexpr int kStackMaxTokens = 4;
+
+struct StackLayout {
+  size_t counters, wsA, wsB, down, act, total;
+};
+
+StackLayout stack_layout(alv_ctx* ctx, const Weight* w) {
+  StackLayout o;
+  o.counters = kHeaderBytes;
+  o.wsA = align_up(o.counters + static_cast<size_t>(w->a.m.RT + w->b.m.RT) * 4, 256);
+  o.wsB = align_up(o.wsA + ws_floats(ctx, w->a.m, kStackMaxTokens) * 4, 256);
+  o.down = align_up(o.wsB + ws_floats(ctx, w->b.m, kStackMaxTokens) * 4, 256);
+  o.act = align_up(o.down + static_cast<size_t>(kStackMaxTokens) * w->H * 4, 256);
+  o.total = align_up(o.act + frag_bytes(w->b.m.KT, kStackMaxTokens), 256);
+  return o;
+}
+
+template <int NT, bool FAST>
+int launch_stack_t(alv_ctx* ctx, StackParams p, cudaStream_t st) {
+  const size_t other = stack_smem_bytes(0, p.gu.KT, p.dn.KT, NT, p.H, p.ntok);
+  p.nst = ring_stages(other);
+  if (!p.nst) return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn_stack: H, I or ntok too large for shared memory");
+  const size_t smem = stack_smem_bytes(p.nst, p.gu.KT, p.dn.KT, NT, p.H, p.ntok);
+  auto k = ffn_stack_kernel<NT, FAST>;
+  int rc = prepare_kernel(ctx, k, smem);
+  if (rc) return rc;
+  k<<<ctx->num_sms, kThreadsPerCta, smem, st>>>(p);
+  ALV_CUDA(ctx, cudaGetLastError());
+  return ALV_OK;
+}
+
+template <bool FAST>
+int launch_stack_f(alv_ctx* ctx, const StackParams& p, uint32_t nt, cudaStream_t st) {
+  switch (nt) {
+    case 1: return launch_stack_t<1, FAST>(ctx, p, st);
+    case 2: return launch_stack_t<2, FAST>(ctx, p, st);
+    case 4: return launch_stack_t<4, FAST>(ctx, p, st);
+  }
+  return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn_stack: unsupported token count");
+}
+}  // namespace
+
+extern "C" int alv_ffn_stack_create(alv_ctx* ctx, const alv_handle* layers, int n, alv_handle* out) {
+  if (!ctx || !layers || !out || n < 1) return fail(ctx, ALV_ERR_ARG, "ffn_stack_create: bad argument");
+  const Weight* w0 = get_weight(ctx, layers[0], 2);
+  if (!w0) return fail(ctx, ALV_ERR_HANDLE, "ffn_stack_create: layer 0 is not an ffn weight");
+  if (w0->i_begin != 0 || w0->i_end != w0->I)
+    return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn_stack_create: layers must hold the whole intermediate dimension");
+  if (w0->H > 32u * kConsumerWarps * kGlueRegs)
+    return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn_stack_create: H must be <= " + std::to_string(32u * kConsumerWarps * kGlueRegs));
+  if (w0->a.m.RT + w0->b.m.RT > kMaxCounters) return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn_stack_create: too large");
+  std::vector<LayerW> lw(static_cast<size_t>(n));
+  for (int l = 0; l < n; ++l) {
+    const Weight* w = get_weight(ctx, layers[l], 2);
+    if (!w) return fail(ctx, ALV_ERR_HANDLE, "ffn_stack_create: layer " + std::to_string(l) + " is not an ffn weight");
+    if (w->H != w0->H || w->I != w0->I || w->i_begin != w0->i_begin || w->i_end != w0->i_end ||
+        w->a.m.fast != w0->a.m.fast)
+      return fail(ctx, ALV_ERR_SHAPE, "ffn_stack_create: layer " + std::to_string(l) +
+                                          " differs in shape or dequant path from layer 0");
+    lw[l] = LayerW{w->a.m.units, w->b.m.units, w->a.m.scale_mul, w->b.m.scale_mul, {0, 0}};
+  }
+  int rc = set_device(ctx);
+  if (rc) return rc;
+  auto s = std::make_unique<Weight>();
+  s->kind = 3;
+  s->a.m = w0->a.m;
+  s->b.m = w0->b.m;
+  s->a.rows = w0->a.rows;
+  s->a.cols = w0->a.cols;
+  s->b.rows = w0->b.rows;
+  s->b.cols = w0->b.cols;
+  s->H = w0->H;
+  s->I = w0->I;
+  s->i_begin = w0->i_begin;
+  s->i_end = w0->i_end;
+  s->act = w0->act;
+  s->layers.assign(layers, layers + n);
+  const StackLayout lo = stack_layout(ctx, s.get());
+  ALV_CUDA(ctx, cudaMalloc(&s->layers_dev, sizeof(LayerW) * lw.size()));
+  ALV_CUDA(ctx, cudaMemcpy(s->layers_dev, lw.data(), sizeof(LayerW) * lw.size(), cudaMemcpyHostToDevice));
+  ALV_CUDA(ctx, cudaMalloc(&s->ws, lo.total));
+  ALV_CUDA(ctx, cudaMemset(s->ws, 0, lo.total));
+  s->ws_bytes = lo.total;
+  ctx->weights.push_back(std::move(s));
+  *out = static_cast<alv_handle>(ctx->weights.size());
+  return ALV_OK;
+}
+
+extern "C" int alv_ffn_stack_run(alv_ctx* ctx, alv_handle h, int ntok, const uint16_t* x_in, uint16_t* out,
+                                 void* stream) {
+  if (!ctx || !x_in || !out) return fail(ctx, ALV_ERR_ARG, "ffn_stack_run: bad argument");
+  Weight* w = get_weight(ctx, h, 3);
+  if (!w) return fail(ctx, ALV_ERR_HANDLE, "ffn_stack_run: invalid handle (not an ffn stack)");
+  if (ntok < 1 || ntok > kStackMaxTokens)
+    return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn_stack_run: ntok must be 1.." + std::to_string(kStackMaxTokens));
+  const Weight* w0 = get_weight(ctx, w->layers[0], 2);
+  if (!w0) return fail(ctx, ALV_ERR_HANDLE, "ffn_stack_run: a layer was destroyed");
+  for (alv_handle lh : w->layers)
+    if (!get_weight(ctx, lh, 2) || get_weight(ctx, lh, 2)->act != w0->act)
+      return fail(ctx, ALV_ERR_ARG, "ffn_stack_run: layers disagree on the activation");
+  int rc = set_device(ctx);
+  if (rc) return rc;
+  const StackLayout lo = stack_layout(ctx, w);
+  StackParams p{};
+  p.layers = w->layers_dev;
+  p.L = static_cast<uint32_t>(w->layers.size());
+  p.gu = w->a.m;
+  p.dn = w->b.m;
+  p.H = w->H;
+  p.I = w->i_end - w->i_begin;
+  p.fn = w0->act;
+  p.ntok = ntok;
+  p.eps = 1e-6f;
+  p.x_in = x_in;
+  p.out = out;
+  p.down = reinterpret_cast<float*>(w->ws + lo.down);
+  p.act = w->ws + lo.act;
+  uint32_t* cnt = reinterpret_cast<uint32_t*>(w->ws + lo.counters);
+  p.fxA = Fixup{reinterpret_cast<float*>(w->ws + lo.wsA), cnt};
+  p.fxB = Fixup{reinterpret_cast<float*>(w->ws + lo.wsB), cnt + w->a.m.RT};
+  p.bar = reinterpret_cast<GridBar*>(w->ws + 256);
+  p.status = reinterpret_cast<uint32_t*>(w->ws);
+  p.trace = ctx->trace;
+  const uint32_t nt = pow2_ceil(static_cast<uint32_t>(ntok));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return p.gu.fast ? launch_stack_f<true>(ctx, p, nt, st) : launch_stack_f<false>(ctx, p, nt, st);
+}
 
 // ===========================================================================
 // Allocation-free gemv.

@@ -10,7 +10,7 @@
 
 namespace alv {
 
-constexpr int kWarpsPerCta = kConsumerWarps;  // consumer warps per CTA (one more warp produces)
+constexpr int kWarpsPerCta = kConsumerWarps;  // warps per CTA, each streaming its own unit range
 
 // ===========================================================================
 // GPU quantizer: restates tools/convert/gemv_q_convert.py:5-85.
@@ -194,9 +194,9 @@ __global__ void q4_dequant_kernel(Q4Mat m, uint32_t rows, uint32_t K, uint16_t* 
     const int b = j >> 1;
     uint32_t a[4];
     if (fast)
-      dequant_word<true>(words[j], S[b][0], C[b][0], S[b][1], C[b][1], a);
+      dequant_word<true>(words[j], S[b][0], C[b][0], S[b][1], C[b][1], bf2_mul(S[b][1], kPow2m4), a);
     else
-      dequant_word<false>(words[j], S[b][0], C[b][0], S[b][1], C[b][1], a);
+      dequant_word<false>(words[j], S[b][0], C[b][0], S[b][1], C[b][1], 0u, a);
     const uint32_t c = kt * 64 + j * 16 + 2 * t4;
     const uint32_t rowv[4] = {r * 16 + g, r * 16 + g + 8, r * 16 + g, r * 16 + g + 8};
     const uint32_t colv[4] = {c, c, c + 8, c + 8};
@@ -363,18 +363,20 @@ __device__ bool grid_barrier(GridBar* gb, uint32_t nblocks, uint32_t* status) {
   return consumers_and(ok != 0);
 }
 
-// Sum over the consumer threads (all of them get the result); red holds >= 32
-// floats.  Fixed order, so every CTA computes the identical value.
+// Sum over the consumer threads (all of them get the result) through `red`
+// (>= 16 floats).  One named barrier: consecutive calls must alternate
+// between two such buffers (a call's buffer is rewritten two calls later,
+// after the intervening call's barrier, when every thread has read it).
+// Fixed order, so every CTA computes the identical value.
 __device__ float consumers_sum(float v, float* red) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  consumers_sync();
   if (lane == 0) red[warp] = v;
   consumers_sync();
   float s = 0.f;
+#pragma unroll
   for (int i = 0; i < kConsumerWarps; ++i) s += red[i];
-  consumers_sync();
   return s;
 }
 
@@ -404,43 +406,46 @@ struct GemvParams {
   uint32_t nst;  // ring stages per warp
 };
 
-constexpr int kUnitsPerStage = 8;
-constexpr int kThreadsPerCta = (kConsumerWarps + 1) * 32;  // consumer warps + 1 producer warp
+constexpr int kUnitsPerStage = ALV_UNITS_PER_STAGE;
+static_assert(kUnitsPerStage % kStageUnroll == 0, "the unroll length must divide the stage");
+constexpr int kThreadsPerCta = kConsumerWarps * 32;
 using Shape = RingShape<kUnitsPerStage>;
 
 __host__ __device__ constexpr size_t ring_smem_bytes(uint32_t nst) { return Shape::smem_bytes(nst); }
+static_assert(ring_smem_bytes(1) % 128 == 0 && ring_smem_bytes(2) % 128 == 0 && ring_smem_bytes(3) % 128 == 0,
+              "what follows the rings must stay 16-byte aligned");
+static_assert(part_bytes(1) % 128 == 0, "what follows the warp partials must stay 16-byte aligned");
+// Shared layout of every streaming kernel: [rings][warp partials][kernel's own].
+__host__ __device__ constexpr size_t base_smem_bytes(uint32_t nst, int ntok) {
+  return ring_smem_bytes(nst) + part_bytes(ntok);
+}
 
 template <int NCOLS, bool SPLIT, bool FAST>
 __global__ void __launch_bounds__(kThreadsPerCta, 1) gemv_kernel(const GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ WorkList wl[kConsumerWarps];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint64_t U = static_cast<uint64_t>(p.m.RT) * p.m.KT;
   const uint64_t W = effective_warps(static_cast<uint64_t>(gridDim.x) * kWarpsPerCta, U, p.m.KT);
   Shape::init_barriers(smem, p.nst);
-  __syncthreads();
-  // Consumer warp c of this CTA (the producer's lane c serves it).
-  const int c = warp < kConsumerWarps ? warp : lane;
-  const uint32_t gw = participant_index(blockIdx.x, static_cast<uint32_t>(c), gridDim.x);
+  const uint32_t gw = participant_index(blockIdx.x, static_cast<uint32_t>(warp));
   uint32_t u0 = 0, u1 = 0;
-  if (c < kConsumerWarps && gw < W) {
+  if (gw < W) {
     u0 = static_cast<uint32_t>(range_start(gw, U, W));
     u1 = static_cast<uint32_t>(range_start(gw + 1, U, W));
   }
-  if (warp == kConsumerWarps) {
-    const WorkList wl{p.m.units + static_cast<size_t>(u0) * kUnitBytes, p.m.units, u1 - u0, 0};
-    producer_wait_release();
-    produce<kUnitsPerStage>(smem, p.nst, wl, l2_policy_evict_first(), p.status);
-    return;
-  }
-  ConsumerRing<kUnitsPerStage> ring;
-  ring.setup(smem, p.nst, warp, u1 - u0);
-  uint8_t* xs = smem + ring_smem_bytes(p.nst);
+  if (lane == 0) wl[warp] = WorkList{p.m.units + static_cast<size_t>(u0) * kUnitBytes, p.m.units, u1 - u0, 0};
+  __syncthreads();
+  ConsumerRing<kUnitsPerStage, WorkList> ring;
+  ring.setup(smem, p.nst, warp, u1 - u0, &wl[warp], p.status);  // weights start streaming
+  Fixup fx = p.fx;
+  fx.part = reinterpret_cast<float*>(smem + ring_smem_bytes(p.nst));
+  uint8_t* xs = smem + base_smem_bytes(p.nst, p.x.ntok);
   stage_frags<NCOLS, SPLIT>(xs, p.m.KT, p.x);
   consumers_sync();
-  consumers_release_producer();
-  if (!consume_range<NCOLS, SPLIT, FAST>(ring, p.m, u0, u1, xs, p.fx, gw, static_cast<uint32_t>(W), p.x.ntok,
-                                         p.epi, p.status))
-    ring.drain(lane);
+  if (!consume_range<NCOLS, SPLIT, FAST>(ring, p.m, u0, u1, xs, fx, p.x.ntok, p.epi, p.status))
+    ring.drain(p.status);
+  cta_fixup(p.m, W, fx, p.x.ntok, p.epi);
 }
 
 // ===========================================================================
@@ -477,61 +482,100 @@ __device__ __forceinline__ void trace_mark(unsigned long long* trace, int i) {
   if (trace && threadIdx.x == 0) trace[blockIdx.x * 16 + i] = globaltimer_ns();
 }
 
-// Glue prologue: build x = bf16(x_in + bf16(rmsnorm(bf16(down_in)))) and
-// xn = bf16(rmsnorm(x)) per token into tmp[ntok][H] (fp32 holding bf16 values).
-// Each consumer thread keeps its share of H in registers, so every global
-// load of a token is in flight at once.  H <= 32 * kConsumerWarps * kGlueRegs.
+// ---------------------------------------------------------------------------
+// Layer glue: the residual update and pre-norm around each FFN call of the
+// decode loop (runtime/py/model.py:782-806, runtime/cpp/src/model.cpp:404),
+// per token
+//   x  = bf16(x_in + bf16(rmsnorm(bf16(d))))   when a down vector d is given
+//   xn = bf16(rmsnorm(x))                       when PRE
+// with unit-weight rmsnorm v / sqrt(mean(v*v) + eps), the mean dividing the
+// float32 sum by H like np.mean.  Consumer thread t owns h = t + i*480
+// (i < GR) and holds them in registers, so every load of a token is in
+// flight at once; sums are reduced in a fixed order, so every caller and
+// every CTA computes identical values.  H <= 480 * GR.
+// ---------------------------------------------------------------------------
 constexpr int kGlueRegs = 16;
 
-// x_src / d_src: the inputs in global or shared memory (d_src may be null).
-__device__ void ffn_glue_prologue(const FfnParams& p, const uint16_t* x_src, const float* d_src, float* tmp,
-                                  float* red) {
+struct Bf16In {   // bf16 values in memory written before the launch (or shared)
+  const uint16_t* p;
+  __device__ __forceinline__ float operator()(size_t i) const { return bf16_bits_to_f32(p[i]); }
+};
+struct F32In {    // fp32 values in memory written before the launch (or shared)
+  const float* p;
+  __device__ __forceinline__ float operator()(size_t i) const { return p[i]; }
+};
+struct F32InL2 {  // fp32 values written earlier in this launch by other CTAs
+  const float* p;
+  __device__ __forceinline__ float operator()(size_t i) const { return __ldcg(p + i); }
+};
+struct NoIn {
+  __device__ __forceinline__ float operator()(size_t) const { return 0.f; }
+};
+struct Bf16Out {  // null: no output
+  uint16_t* p;
+  __device__ __forceinline__ void operator()(size_t i, float v) const {
+    if (p) p[i] = bf16_bits_rn(v);
+  }
+};
+
+// xn (PRE) goes to xn_out[ntok][H] (fp32 holding bf16 values).
+template <int GR, bool PRE, bool HAS_D, class XL, class DL, class XO>
+__device__ void glue_tokens(int ntok, uint32_t H, float eps, const XL& xl, const DL& dl, const XO& xo,
+                            float* xn_out, float* red) {
   constexpr uint32_t NTHR = kConsumerWarps * 32;
-  const uint32_t H = p.H;
-  const float hf = static_cast<float>(H);  // np.mean divides the float32 sum by n
-  for (int tok = 0; tok < p.ntok; ++tok) {
-    const uint16_t* xi = x_src + static_cast<size_t>(tok) * H;
-    const float* di = d_src ? d_src + static_cast<size_t>(tok) * H : nullptr;
-    float xv[kGlueRegs], dv[kGlueRegs];
+  static_assert(kConsumerWarps <= 16, "consumers_sum buffers hold 16 partials");
+  const float hf = static_cast<float>(H);
+  // consumers_sum alternates between red[0..15] and red[16..31]; the caller's
+  // barrier before the glue orders this glue's first use after the last one
+  // of the previous glue.
+  int rs = 0;
+  for (int tok = 0; tok < ntok; ++tok) {
+    const size_t base = static_cast<size_t>(tok) * H;
+    float xv[GR], dv[GR];
 #pragma unroll
-    for (int i = 0; i < kGlueRegs; ++i) {
+    for (int i = 0; i < GR; ++i) {
       const uint32_t h = threadIdx.x + i * NTHR;
-      xv[i] = h < H ? bf16_bits_to_f32(xi[h]) : 0.f;
-      dv[i] = (di && h < H) ? bf16_round(di[h]) : 0.f;
+      xv[i] = h < H ? xl(base + h) : 0.f;
+      dv[i] = (HAS_D && h < H) ? bf16_round(dl(base + h)) : 0.f;
     }
-    if (di) {
+    if (HAS_D) {
       float ss = 0.f;
 #pragma unroll
-      for (int i = 0; i < kGlueRegs; ++i) ss = fmaf(dv[i], dv[i], ss);
-      ss = consumers_sum(ss, red);
-      trace_mark(p.trace, 8);
-      const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, hf), p.eps)));
+      for (int i = 0; i < GR; ++i) ss = fmaf(dv[i], dv[i], ss);
+      ss = consumers_sum(ss, red + 16 * (rs++ & 1));
+      const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, hf), eps)));
 #pragma unroll
-      for (int i = 0; i < kGlueRegs; ++i) xv[i] = bf16_round(xv[i] + bf16_round(dv[i] * inv));
-      trace_mark(p.trace, 9);
+      for (int i = 0; i < GR; ++i) xv[i] = bf16_round(xv[i] + bf16_round(dv[i] * inv));
     }
-    if (blockIdx.x == 0 && p.x_out) {
 #pragma unroll
-      for (int i = 0; i < kGlueRegs; ++i) {
-        const uint32_t h = threadIdx.x + i * NTHR;
-        if (h < H) p.x_out[static_cast<size_t>(tok) * H + h] = bf16_bits_rn(xv[i]);
-      }
-    }
-    float ss = 0.f;
-#pragma unroll
-    for (int i = 0; i < kGlueRegs; ++i) ss = fmaf(xv[i], xv[i], ss);
-    trace_mark(p.trace, 10);
-    ss = consumers_sum(ss, red);
-    trace_mark(p.trace, 11);
-    const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, hf), p.eps)));
-    float* xt = tmp + static_cast<size_t>(tok) * H;
-#pragma unroll
-    for (int i = 0; i < kGlueRegs; ++i) {
+    for (int i = 0; i < GR; ++i) {
       const uint32_t h = threadIdx.x + i * NTHR;
-      if (h < H) xt[h] = bf16_round(xv[i] * inv);
+      if (h < H) xo(base + h, xv[i]);
+    }
+    if (PRE) {
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < GR; ++i) ss = fmaf(xv[i], xv[i], ss);
+      ss = consumers_sum(ss, red + 16 * (rs++ & 1));
+      const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, hf), eps)));
+#pragma unroll
+      for (int i = 0; i < GR; ++i) {
+        const uint32_t h = threadIdx.x + i * NTHR;
+        if (h < H) xn_out[base + h] = bf16_round(xv[i] * inv);
+      }
     }
   }
   consumers_sync();
+}
+
+// GR chosen from H at run time (8 covers H <= 3840).
+template <bool PRE, bool HAS_D, class XL, class DL, class XO>
+__device__ __forceinline__ void glue(int ntok, uint32_t H, float eps, const XL& xl, const DL& dl, const XO& xo,
+                                     float* xn_out, float* red) {
+  if (H <= 8u * kConsumerWarps * 32)
+    glue_tokens<8, PRE, HAS_D>(ntok, H, eps, xl, dl, xo, xn_out, red);
+  else
+    glue_tokens<kGlueRegs, PRE, HAS_D>(ntok, H, eps, xl, dl, xo, xn_out, red);
 }
 
 template <int NT, bool SPLIT, bool FAST>
@@ -545,21 +589,26 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_kernel(const FfnParams 
   const uint64_t UA = static_cast<uint64_t>(p.gu.RT) * p.gu.KT;
   const uint64_t UB = static_cast<uint64_t>(p.dn.RT) * p.dn.KT;
   const uint64_t WA = effective_warps(Wtot, UA, p.gu.KT), WB = effective_warps(Wtot, UB, p.dn.KT);
+  __shared__ WorkList wl[kConsumerWarps];
   Shape::init_barriers(smem, p.nst);
-  __syncthreads();
-  const int c = warp < kConsumerWarps ? warp : lane;
-  const uint32_t gw = participant_index(blockIdx.x, static_cast<uint32_t>(c), gridDim.x);
+  const uint32_t gw = participant_index(blockIdx.x, static_cast<uint32_t>(warp));
   uint32_t a0 = 0, a1 = 0, b0 = 0, b1 = 0;
-  if (c < kConsumerWarps && gw < WA) {
+  if (gw < WA) {
     a0 = static_cast<uint32_t>(range_start(gw, UA, WA));
     a1 = static_cast<uint32_t>(range_start(gw + 1, UA, WA));
   }
-  if (c < kConsumerWarps && gw < WB) {
+  if (gw < WB) {
     b0 = static_cast<uint32_t>(range_start(gw, UB, WB));
     b1 = static_cast<uint32_t>(range_start(gw + 1, UB, WB));
   }
-  // Shared layout after the rings: [xs frags][red][tmp ntok*H f32][x_in raw][down_in raw][xbar]
-  uint8_t* xs = smem + ring_smem_bytes(p.nst);
+  if (lane == 0)
+    wl[warp] = WorkList{p.gu.units + static_cast<size_t>(a0) * kUnitBytes,
+                        p.dn.units + static_cast<size_t>(b0) * kUnitBytes, a1 - a0, b1 - b0};
+  // Shared layout after the rings and warp partials:
+  // [xs frags][red][tmp ntok*H f32][x_in raw][down_in raw][xbar]
+  Fixup fxA = p.fxA, fxB = p.fxB;
+  fxA.part = fxB.part = reinterpret_cast<float*>(smem + ring_smem_bytes(p.nst));
+  uint8_t* xs = smem + base_smem_bytes(p.nst, p.ntok);
   const size_t xs_bytes_a = frag_bytes(p.gu.KT, NCA);
   const size_t xs_bytes_b = frag_bytes(p.dn.KT, NCB);
   const size_t xs_bytes = xs_bytes_a > xs_bytes_b ? xs_bytes_a : xs_bytes_b;
@@ -575,26 +624,16 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_kernel(const FfnParams 
     fence_mbar_init();
   }
   __syncthreads();
-  if (warp == kConsumerWarps) {
-    const WorkList wl{p.gu.units + static_cast<size_t>(a0) * kUnitBytes,
-                      p.dn.units + static_cast<size_t>(b0) * kUnitBytes, a1 - a0, b1 - b0};
+  if (tma_in && threadIdx.x == 0) {
+    // The layer inputs go first, ahead of the weight stream.
     const uint64_t pol = l2_policy_evict_first();
-    if (tma_in) {
-      // The layer inputs go first, ahead of the weight stream.
-      if (lane == 0) {
-        const uint32_t xb = static_cast<uint32_t>(glue_vals * 2), db = p.down_in ? static_cast<uint32_t>(glue_vals * 4) : 0;
-        mbar_arrive_expect_tx(xbar, xb + db);
-        bulk_g2s(xraw, p.x_in, xb, xbar, pol);
-        if (db) bulk_g2s(draw, p.down_in, db, xbar, pol);
-      }
-    } else {
-      producer_wait_release();
-    }
-    produce<kUnitsPerStage>(smem, p.nst, wl, pol, p.status);
-    return;
+    const uint32_t xb = static_cast<uint32_t>(glue_vals * 2), db = p.down_in ? static_cast<uint32_t>(glue_vals * 4) : 0;
+    mbar_arrive_expect_tx(xbar, xb + db);
+    bulk_g2s(xraw, p.x_in, xb, xbar, pol);
+    if (db) bulk_g2s(draw, p.down_in, db, xbar, pol);
   }
-  ConsumerRing<kUnitsPerStage> ring;
-  ring.setup(smem, p.nst, warp, (a1 - a0) + (b1 - b0));
+  ConsumerRing<kUnitsPerStage, WorkList> ring;
+  ring.setup(smem, p.nst, warp, (a1 - a0) + (b1 - b0), &wl[warp], p.status);
   trace_mark(p.trace, 0);
 
   // The act padding (k in [I, 64*dn.KT)) must read as zero in phase B.
@@ -610,19 +649,23 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_kernel(const FfnParams 
     if (tma_in) in_ok = consumers_and(mbar_wait_bounded(xbar, 0));
     if (!in_ok && threadIdx.x == 0) atomicOr(p.status, kStatusMbarTimeout);
     trace_mark(p.trace, 6);
-    ffn_glue_prologue(p, tma_in ? xraw : p.x_in, tma_in ? (p.down_in ? draw : nullptr) : p.down_in, tmp, red);
+    const Bf16Out xo{blockIdx.x == 0 ? p.x_out : nullptr};
+    const Bf16In xl{tma_in ? xraw : p.x_in};
+    if (p.down_in)
+      glue<true, true>(p.ntok, p.H, p.eps, xl, F32In{tma_in ? draw : p.down_in}, xo, tmp, red);
+    else
+      glue<true, false>(p.ntok, p.H, p.eps, xl, NoIn{}, xo, tmp, red);
     trace_mark(p.trace, 7);
     stage_frags<NCA, false>(xs, p.gu.KT, SmemSrc{tmp, p.ntok, p.H});
   } else {
     stage_frags<NCA, SPLIT>(xs, p.gu.KT, p.x);
   }
   consumers_sync();
-  if (!tma_in) consumers_release_producer();
   trace_mark(p.trace, 1);
 
   GateUpEpi ge{p.act, p.I, NCB, p.gu.scale_mul, p.fn};
-  const bool ok = consume_range<NCA, SPLIT, FAST>(ring, p.gu, a0, a1, xs, p.fxA, gw, static_cast<uint32_t>(WA),
-                                                  p.ntok, ge, p.status);
+  const bool ok = consume_range<NCA, SPLIT, FAST>(ring, p.gu, a0, a1, xs, fxA, p.ntok, ge, p.status);
+  cta_fixup(p.gu, WA, fxA, p.ntok, ge);
   if (p.trace) {
     consumers_sync();
     trace_mark(p.trace, 2);
@@ -630,7 +673,7 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_kernel(const FfnParams 
   const bool bar_ok = grid_barrier(p.bar, gridDim.x, p.status);
   trace_mark(p.trace, 3);
   if (!bar_ok || !consumers_and(ok)) {
-    ring.drain(lane);
+    ring.drain(p.status);
     return;
   }
   // act is already in fragment order: stage it with 16-byte copies through L2.
@@ -638,36 +681,173 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_kernel(const FfnParams 
     *reinterpret_cast<uint4*>(xs + o) = __ldcg(reinterpret_cast<const uint4*>(p.act + o));
   consumers_sync();
   trace_mark(p.trace, 4);
-  if (!consume_range<NCB, false, FAST>(ring, p.dn, b0, b1, xs, p.fxB, gw, static_cast<uint32_t>(WB), p.ntok,
-                                       p.out, p.status))
-    ring.drain(lane);
+  if (!consume_range<NCB, false, FAST>(ring, p.dn, b0, b1, xs, fxB, p.ntok, p.out, p.status))
+    ring.drain(p.status);
+  cta_fixup(p.dn, WB, fxB, p.ntok, p.out);
   if (p.trace) {
     consumers_sync();
     trace_mark(p.trace, 5);
   }
 }
 
-// Final residual of an FFN stack (single CTA).
-__global__ void ffn_stack_finalize_kernel(int ntok, uint32_t H, const uint16_t* x_in,
-                                          const float* down_in, uint16_t* x_out, float eps) {
-  __shared__ float red[32];
-  const float hf = static_cast<float>(H);
-  for (int tok = 0; tok < ntok; ++tok) {
-    const float* di = down_in + static_cast<size_t>(tok) * H;
-    const uint16_t* xi = x_in + static_cast<size_t>(tok) * H;
-    float ss = 0.f;
-    for (uint32_t h = threadIdx.x; h < H; h += blockDim.x) {
-      const float d = bf16_round(di[h]);
-      ss = fmaf(d, d, ss);
+// ===========================================================================
+// Whole FFN stack in one persistent launch: for l = 0..L-1
+//   glue (x += rmsnorm(down_{l-1}); xn = rmsnorm(x)) -> phase A (gate/up +
+//   activation -> act) -> grid barrier -> phase B (down -> down_l) -> grid
+//   barrier,
+// then the last residual x += rmsnorm(down_{L-1}) -> out.  Each warp's ring
+// runs through every layer's weights back to back, so nst groups stay in
+// flight while the warps run the glue and wait at the barriers.  The residual
+// stream stays in shared memory (every CTA holds the identical copy); only
+// down (H fp32 per token) and act cross CTAs, through L2.  Each step's
+// arithmetic and reduction order equal the per-layer ffn_kernel chain, so
+// the two paths agree bit for bit.
+// ===========================================================================
+struct StackParams {
+  const LayerW* layers;
+  uint32_t L;
+  Q4Mat gu, dn;           // per-layer shapes (RT, KT); units / scale_mul come from layers
+  uint32_t H, I;
+  int fn;
+  int ntok;
+  float eps;
+  const uint16_t* x_in;   // [ntok][H] bf16 stack input
+  uint16_t* out;          // [ntok][H] bf16 stack output
+  float* down;            // [ntok][H] fp32: a layer's down projection
+  uint8_t* act;           // [dn.KT*64][ntok] bf16 intermediate, B-fragment order
+  Fixup fxA, fxB;
+  GridBar* bar;
+  uint32_t* status;
+  uint32_t nst;
+  unsigned long long* trace;  // optional: phase stamps of layer 1
+};
+
+// Epilogue of either stack phase: gate/up -> activation into act (phase A),
+// or down rows into the fp32 down vector (phase B).
+struct StackEpi {
+  bool down_phase;
+  uint8_t* act;
+  float* down;
+  uint32_t I, H, ncb;
+  float sm;
+  int fn;
+  __device__ __forceinline__ void apply(uint32_t r, int g, int tok, float vg, float vg8) const {
+    if (down_phase) {
+      RowsEpi{down, nullptr, H, H, sm}.apply(r, g, tok, vg, vg8);
+    } else {
+      GateUpEpi{act, I, ncb, sm, fn}.apply(r, g, tok, vg, vg8);
     }
-    ss = block_sum(ss, red);
-    const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, hf), eps)));
-    for (uint32_t h = threadIdx.x; h < H; h += blockDim.x) {
-      const float dn = bf16_round(bf16_round(di[h]) * inv);
-      x_out[static_cast<size_t>(tok) * H + h] = bf16_bits_rn(bf16_bits_to_f32(xi[h]) + dn);
-    }
-    __syncthreads();
   }
+};
+
+// Shared layout after the rings: [xs region][red 32 f][xres ntok*H bf16].
+// The xs region holds phase B's fragments, or phase A's fragments followed by
+// the glue's xn (tmp, fp32).
+__host__ __device__ inline size_t stack_xs_region(uint32_t KTA, uint32_t KTB, int nc, uint32_t H, int ntok) {
+  const size_t b = frag_bytes(KTB, nc);
+  const size_t a = frag_bytes(KTA, nc) + static_cast<size_t>(ntok) * H * 4;
+  return ((b > a ? b : a) + 15) / 16 * 16;
+}
+__host__ __device__ inline size_t stack_smem_bytes(uint32_t nst, uint32_t KTA, uint32_t KTB, int nc, uint32_t H,
+                                                   int ntok) {
+  return base_smem_bytes(nst, ntok) + stack_xs_region(KTA, KTB, nc, H, ntok) + 128 + static_cast<size_t>(ntok) * H * 2;
+}
+
+template <int NT, bool FAST>
+__global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const StackParams p) {
+  constexpr int NC = NT;  // bf16 activations: one fragment column per token
+  constexpr uint32_t NTHR = kConsumerWarps * 32;
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint32_t wk[kConsumerWarps][8];  // per warp: a0 a1 b0 b1 gw WA WB
+  __shared__ StackWork sw[kConsumerWarps];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  Shape::init_barriers(smem, p.nst);
+  if (lane == 0) {
+    const uint64_t Wtot = static_cast<uint64_t>(gridDim.x) * kWarpsPerCta;
+    const uint64_t UA = static_cast<uint64_t>(p.gu.RT) * p.gu.KT;
+    const uint64_t UB = static_cast<uint64_t>(p.dn.RT) * p.dn.KT;
+    const uint64_t WA = effective_warps(Wtot, UA, p.gu.KT), WB = effective_warps(Wtot, UB, p.dn.KT);
+    const uint32_t gw = participant_index(blockIdx.x, static_cast<uint32_t>(warp));
+    uint32_t a0 = 0, a1 = 0, b0 = 0, b1 = 0;
+    if (gw < WA) {
+      a0 = static_cast<uint32_t>(range_start(gw, UA, WA));
+      a1 = static_cast<uint32_t>(range_start(gw + 1, UA, WA));
+    }
+    if (gw < WB) {
+      b0 = static_cast<uint32_t>(range_start(gw, UB, WB));
+      b1 = static_cast<uint32_t>(range_start(gw + 1, UB, WB));
+    }
+    uint32_t* w = wk[warp];
+    w[0] = a0; w[1] = a1; w[2] = b0; w[3] = b1;
+    w[4] = gw; w[5] = static_cast<uint32_t>(WA); w[6] = static_cast<uint32_t>(WB);
+    sw[warp] = StackWork{p.layers, p.L, a0, a1 - a0, b0, b1 - b0};
+  }
+  __syncthreads();
+  const uint32_t* my = wk[warp];
+  ConsumerRing<kUnitsPerStage, StackWork> ring;
+  ring.setup(smem, p.nst, warp, p.L * ((my[1] - my[0]) + (my[3] - my[2])), &sw[warp], p.status);
+  // The act padding (k in [I, 64*dn.KT)) must read as zero in phase B.
+  if (blockIdx.x == 0) {
+    const uint32_t kpad = p.dn.KT * 64;
+    for (uint32_t e = threadIdx.x; e < (kpad - p.I) * NC; e += NTHR) {
+      const uint32_t n = e % NC, k = p.I + e / NC;
+      *reinterpret_cast<uint16_t*>(p.act + frag_offset(NC, n, k)) = 0;
+    }
+  }
+#pragma unroll 1
+  for (uint32_t i = 0; i < 2 * p.L; ++i) {
+    const uint32_t l = i >> 1;
+    const bool B = i & 1;
+    uint8_t* xs = smem + base_smem_bytes(p.nst, p.ntok);
+    unsigned long long* tr = (l == 1) ? p.trace : nullptr;
+    if (!B) {
+      float* tmp = reinterpret_cast<float*>(xs + frag_bytes(p.gu.KT, NC));
+      float* red = reinterpret_cast<float*>(xs + stack_xs_region(p.gu.KT, p.dn.KT, NC, p.H, p.ntok));
+      uint16_t* xres = reinterpret_cast<uint16_t*>(red + 32);  // the residual stream (bf16)
+      trace_mark(tr, 0);
+      if (l == 0)
+        glue<true, false>(p.ntok, p.H, p.eps, Bf16In{p.x_in}, NoIn{}, Bf16Out{xres}, tmp, red);
+      else
+        glue<true, true>(p.ntok, p.H, p.eps, Bf16In{xres}, F32InL2{p.down}, Bf16Out{xres}, tmp, red);
+      stage_frags<NC, false>(xs, p.gu.KT, SmemSrc{tmp, p.ntok, p.H});
+    } else {
+      const uint32_t xs_b = static_cast<uint32_t>(frag_bytes(p.dn.KT, NC));
+      for (uint32_t o = threadIdx.x * 16; o < xs_b; o += NTHR * 16)
+        *reinterpret_cast<uint4*>(xs + o) = __ldcg(reinterpret_cast<const uint4*>(p.act + o));
+    }
+    consumers_sync();
+    trace_mark(tr, B ? 4 : 1);
+    const StackEpi epi{B, p.act, p.down, p.I, p.H, NC, B ? __ldg(&p.layers[l].dn_mul) : __ldg(&p.layers[l].gu_mul), p.fn};
+    Fixup fx = B ? p.fxB : p.fxA;
+    fx.part = reinterpret_cast<float*>(smem + ring_smem_bytes(p.nst));
+    const bool ok = consume_range<NC, false, FAST>(ring, B ? p.dn : p.gu, my[B ? 2 : 0], my[B ? 3 : 1], xs, fx,
+                                                   p.ntok, epi, p.status);
+    cta_fixup(B ? p.dn : p.gu, my[B ? 6 : 5], fx, p.ntok, epi);
+    if (tr) {
+      consumers_sync();
+      trace_mark(tr, B ? 5 : 2);
+    }
+    if (!grid_barrier(p.bar, gridDim.x, p.status) || !consumers_and(ok)) {
+      ring.drain(p.status);
+      return;
+    }
+    trace_mark(tr, B ? 6 : 3);
+  }
+  if (blockIdx.x == 0) {
+    float* red = reinterpret_cast<float*>(smem + base_smem_bytes(p.nst, p.ntok) +
+                                          stack_xs_region(p.gu.KT, p.dn.KT, NC, p.H, p.ntok));
+    glue<false, true>(p.ntok, p.H, p.eps, Bf16In{reinterpret_cast<uint16_t*>(red + 32)}, F32InL2{p.down},
+                      Bf16Out{p.out}, nullptr, red);
+  }
+}
+
+// Final residual of an FFN stack: one CTA of 480 threads (the glue's thread
+// layout, so the sums match the in-kernel glue bit for bit).
+__global__ void __launch_bounds__(kConsumerWarps * 32, 1)
+    ffn_stack_finalize_kernel(int ntok, uint32_t H, const uint16_t* x_in, const float* down_in, uint16_t* x_out,
+                              float eps) {
+  __shared__ float red[32];
+  glue<false, true>(ntok, H, eps, Bf16In{x_in}, F32In{down_in}, Bf16Out{x_out}, nullptr, red);
 }
 
 }  // namespace alv

@@ -40,7 +40,17 @@ constexpr int kUnitBytes = 576;
 constexpr int kUnitNibBytes = 512;
 constexpr int kTileRows = 16;
 constexpr int kTileCols = 64;
-constexpr int kConsumerWarps = 15;  // + 1 producer warp = 16 warps, 4 per SM sub-partition
+// Units per ring stage (one bulk-copy group).
+#ifndef ALV_UNITS_PER_STAGE
+#define ALV_UNITS_PER_STAGE 8
+#endif
+
+// Warps per CTA (one CTA per SM), each streaming its own unit range.
+#ifndef ALV_WARPS
+#define ALV_WARPS 15
+#endif
+constexpr int kConsumerWarps = ALV_WARPS;
+constexpr uint32_t kWarpsPerCtaS = kConsumerWarps;
 
 struct Q4Mat {
   const uint8_t* units;  // RT*KT units of kUnitBytes
@@ -51,8 +61,8 @@ struct Q4Mat {
 };
 
 // Contiguous split of U units over W warps: warp w owns [start(w), start(w+1)).
-// W must be min(#warps, U) so that every participating warp owns >= 1 unit
-// (the fixup counts contributors as a contiguous warp interval).
+// W <= U, so every participating warp owns >= 1 unit (the fixup counts
+// contributors as contiguous warp and CTA intervals).
 __device__ __forceinline__ uint64_t range_start(uint64_t w, uint64_t U, uint64_t W) {
   return w * U / W;
 }
@@ -65,10 +75,11 @@ __host__ __device__ __forceinline__ uint64_t effective_warps(uint64_t Wtot, uint
   if (w < 1) w = 1;
   return w < Wtot ? w : Wtot;
 }
-// Participating warp index of warp `warp` of CTA `cta`: warp-major over CTAs,
-// so a small problem spreads over all SMs.
-__device__ __forceinline__ uint32_t participant_index(uint32_t cta, uint32_t warp, uint32_t nctas) {
-  return warp * nctas + cta;
+// Participating warp index of warp `warp` of CTA `cta`: CTA-major, so a CTA
+// owns one contiguous unit range and a row tile split between its warps is
+// reduced in shared memory.
+__device__ __forceinline__ uint32_t participant_index(uint32_t cta, uint32_t warp) {
+  return cta * kWarpsPerCtaS + warp;
 }
 // The warp whose range contains unit u.
 __device__ __forceinline__ uint32_t warp_of_unit(uint64_t u, uint64_t U, uint64_t W) {
@@ -77,19 +88,28 @@ __device__ __forceinline__ uint32_t warp_of_unit(uint64_t u, uint64_t U, uint64_
 
 // ---------------------------------------------------------------------------
 // Dequantize one 32-bit nibble word into the four bf16x2 A-fragment registers.
-// S*/C* are bf16x2 broadcasts of the scale (and -8*scale) for rows g and g+8.
+// S*/C* are bf16x2 broadcasts of the scale (and -8*scale) for rows g and g+8;
+// S16g8 is the fast-path scale of row g+8 times 2^-4.
+//
+// Fast path: bits 0-7 of a bf16 half, read as an integer v, encode the value
+// v * 2^-133 whether bit 7 (the exponent's lowest bit) is set or not, so a
+// nibble masked in place at bits 0-3 is u * 2^-133 and one at bits 4-7 is
+// 16u * 2^-133.  The first pairs with S, the second with S/16 (an exact
+// power-of-two rescale), and one shift by 8 brings the upper two nibbles down:
+// one shift and four masks per word instead of three shifts and four masks.
 // ---------------------------------------------------------------------------
 template <bool FAST>
-__device__ __forceinline__ void dequant_word(uint32_t w, uint32_t Sg, uint32_t Cg, uint32_t Sg8,
-                                             uint32_t Cg8, uint32_t (&a)[4]) {
+__device__ __forceinline__ void dequant_word(uint32_t w, uint32_t Sg, uint32_t Cg, uint32_t Sg8, uint32_t Cg8,
+                                             uint32_t S16g8, uint32_t (&a)[4]) {
   const uint32_t m = 0x000F000Fu;
-  const uint32_t p0 = w & m, p1 = (w >> 4) & m, p2 = (w >> 8) & m, p3 = (w >> 12) & m;
   if (FAST) {
-    a[0] = bf2_fma(p0, Sg, Cg);
-    a[1] = bf2_fma(p1, Sg8, Cg8);
-    a[2] = bf2_fma(p2, Sg, Cg);
-    a[3] = bf2_fma(p3, Sg8, Cg8);
+    const uint32_t w8 = w >> 8;
+    a[0] = bf2_fma(w & m, Sg, Cg);
+    a[1] = bf2_fma(w & (m << 4), S16g8, Cg8);
+    a[2] = bf2_fma(w8 & m, Sg, Cg);
+    a[3] = bf2_fma(w8 & (m << 4), S16g8, Cg8);
   } else {
+    const uint32_t p0 = w & m, p1 = (w >> 4) & m, p2 = (w >> 8) & m, p3 = (w >> 12) & m;
     const uint32_t magic = 0x43004300u;   // bf16x2 (128, 128)
     const uint32_t m136 = 0x43084308u;    // bf16x2 (136, 136)
     a[0] = bf2_mul(bf2_sub(p0 | magic, m136), Sg);
@@ -98,6 +118,9 @@ __device__ __forceinline__ void dequant_word(uint32_t w, uint32_t Sg, uint32_t C
     a[3] = bf2_mul(bf2_sub(p3 | magic, m136), Sg8);
   }
 }
+
+// bf16x2 (2^-4, 2^-4)
+constexpr uint32_t kPow2m4 = 0x3D803D80u;
 
 // bf16x2 (-2^-130, -2^-130): multiplying a fast-path stored scale by it gives -8*s*2^-je.
 constexpr uint32_t kNeg8Sub = 0x80088008u;
@@ -155,28 +178,64 @@ __host__ __device__ constexpr size_t frag_bytes(uint32_t KT, int ncols) {
 }
 
 // ---------------------------------------------------------------------------
-// Warp-specialized unit rings.  Each consumer warp of a CTA owns a ring of
-// nst stages of UPS units; one more warp (the producer) fills them with
-// 1-D bulk copies through the TMA engine.  Per stage: `full` (producer
-// arrive.expect_tx, completed by the copy) and `empty` (consumer lane 0
-// arrives after the stage's data has been read and used).  A consumer's work
-// list is up to two contiguous unit ranges (segment 0 then segment 1, e.g.
-// FFN gate/up then down); a stage may straddle them.
+// Per-warp unit rings.  Each warp of a CTA owns a ring of nst stages of UPS
+// units in shared memory, filled by 1-D bulk copies through the TMA engine
+// (one `full` mbarrier per stage: arrive.expect_tx, completed by the copies).
+// The warp refills its own ring: when it has used a stage, its lane 0 issues
+// the copies of the group nst groups ahead into that stage, so nst groups
+// are always in flight and no warp spends issue slots polling.  A warp's
+// work is a sequence of contiguous unit ranges (segments: e.g. FFN gate/up
+// then down, layer after layer); groups of UPS units are cut from the
+// concatenated sequence, so a stage may span segment ends.
 // ---------------------------------------------------------------------------
 
-// Work list of one consumer warp.
+// Work of one warp as two segments (segment 0 then segment 1).
 struct WorkList {
   const uint8_t* s0;   // first unit of segment 0
   const uint8_t* s1;   // first unit of segment 1
   uint32_t c0, c1;     // units in each segment
+  __device__ uint32_t nseg() const { return 2; }
+  __device__ void get(uint32_t i, const uint8_t*& base, uint32_t& n) const {
+    base = i ? s1 : s0;
+    n = i ? c1 : c0;
+  }
 };
 
+// Per-layer weights of a fused FFN stack.
+struct LayerW {
+  const uint8_t* gu;   // gate/up units of the layer
+  const uint8_t* dn;   // down units
+  float gu_mul, dn_mul;  // dequant epilogue multipliers (2^je, or 1)
+  uint32_t pad[2];
+};
+
+// Work of one warp over a whole FFN stack: layer l contributes gate/up units
+// [a0, a0+na) then down units [b0, b0+nb).
+struct StackWork {
+  const LayerW* layers;
+  uint32_t L, a0, na, b0, nb;
+  __device__ uint32_t nseg() const { return 2 * L; }
+  __device__ void get(uint32_t i, const uint8_t*& base, uint32_t& n) const {
+    const LayerW* lw = layers + (i >> 1);
+    if (i & 1) {
+      base = reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(&lw->dn))) +
+             static_cast<size_t>(b0) * kUnitBytes;
+      n = nb;
+    } else {
+      base = reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(&lw->gu))) +
+             static_cast<size_t>(a0) * kUnitBytes;
+      n = na;
+    }
+  }
+};
+
+// [rings: warps x nst x stage][full barriers: warps x nst], padded to 128
+// bytes so whatever follows keeps 16-byte (vector / bulk copy) alignment.
 template <int UPS>
 struct RingShape {
   static constexpr uint32_t kStageBytes = UPS * kUnitBytes;
-  // [rings: consumers x nst x stage][full: consumers x nst][empty: consumers x nst]
   __host__ __device__ static constexpr size_t smem_bytes(uint32_t nst) {
-    return static_cast<size_t>(kConsumerWarps) * nst * (kStageBytes + 16);
+    return (static_cast<size_t>(kConsumerWarps) * nst * (kStageBytes + 8) + 127) / 128 * 128;
   }
   __device__ static uint8_t* ring(uint8_t* smem, uint32_t nst, int c) {
     return smem + static_cast<size_t>(c) * nst * kStageBytes;
@@ -184,43 +243,120 @@ struct RingShape {
   __device__ static uint64_t* full(uint8_t* smem, uint32_t nst, int c) {
     return reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(kConsumerWarps) * nst * kStageBytes) + c * nst;
   }
-  __device__ static uint64_t* empty(uint8_t* smem, uint32_t nst, int c) {
-    return full(smem, nst, c) + kConsumerWarps * nst;
-  }
   // All threads: initialize every barrier, then the caller syncs the CTA.
   __device__ static void init_barriers(uint8_t* smem, uint32_t nst) {
     uint64_t* f = full(smem, nst, 0);
-    for (uint32_t i = threadIdx.x; i < 2u * kConsumerWarps * nst; i += blockDim.x) mbar_init(&f[i], 1);
+    for (uint32_t i = threadIdx.x; i < kConsumerWarps * nst; i += blockDim.x) mbar_init(&f[i], 1);
     fence_mbar_init();
   }
 };
 
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+// Lane 0 only (pred): arm `bar` for `bytes` and start one bulk copy into it.
+__device__ __forceinline__ void lane0_arm_and_copy(bool pred, uint32_t bar, uint32_t bytes, uint32_t dst,
+                                                   const void* src, uint32_t copy_bytes, uint64_t policy) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.u32 p, %0, 0;\n\t"
+      "@p mbarrier.arrive.expect_tx.shared::cta.b64 _, [%1], %2;\n\t"
+      "@p cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%3], [%4], %5, [%1], %6;\n\t}" ::"r"(static_cast<uint32_t>(pred)),
+      "r"(bar), "r"(bytes), "r"(dst), "l"(src), "r"(copy_bytes), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ void lane0_copy(bool pred, uint32_t bar, uint32_t dst, const void* src,
+                                           uint32_t copy_bytes, uint64_t policy) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.u32 p, %0, 0;\n\t"
+      "@p cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%2], [%3], %4, [%1], %5;\n\t}" ::"r"(static_cast<uint32_t>(pred)),
+      "r"(bar), "r"(dst), "l"(src), "r"(copy_bytes), "l"(policy)
+      : "memory");
 }
 
-// Consumer side.
-template <int UPS>
+// Copy cursor state passed by value to the out-of-line multi-piece refill.
+struct Cursor {
+  const uint8_t* src;
+  uint32_t seg_left, si;
+};
+
+// Rare path of a refill: the group spans segment ends (or starts the
+// sequence).  Arms `bar` for n units and copies them piece by piece, each
+// piece inside its segment by construction.
+template <class Seq>
+__device__ __noinline__ Cursor refill_pieces(Cursor c, const Seq* seq, uint32_t dst, uint32_t bar, uint32_t n,
+                                             bool l0, uint64_t policy, uint32_t* status) {
+  if (l0) mbar_arrive_expect_tx_s(bar, n * kUnitBytes);
+  const Seq sq = *seq;
+  const uint32_t nseg = sq.nseg();
+  uint32_t k = 0;
+  while (k < n) {
+    while (c.seg_left == 0 && c.si < nseg) sq.get(c.si++, c.src, c.seg_left);
+    if (c.seg_left == 0) break;  // cannot happen: n <= units left in the sequence
+    const uint32_t m = (n - k) < c.seg_left ? (n - k) : c.seg_left;
+    lane0_copy(l0, bar, dst + k * kUnitBytes, c.src, m * kUnitBytes, policy);
+    c.src += static_cast<size_t>(m) * kUnitBytes;
+    c.seg_left -= m;
+    k += m;
+  }
+  if (k != n && l0) atomicOr(status, kStatusBadLaunch);  // the stage's wait will time out
+  return c;
+}
+
+// One warp's ring.  The copy cursor lives in registers and is updated by all
+// lanes alike (uniform control flow); lane 0 alone issues the copies.
+template <int UPS, class Seq>
 struct ConsumerRing {
   static constexpr uint32_t kStageBytes = UPS * kUnitBytes;
   uint32_t ring_saddr;      // shared address of this warp's ring
-  uint64_t* full;
-  uint64_t* empty;
+  uint32_t full_saddr;      // shared address of this warp's full[0]
   uint32_t nst;
   uint32_t stage, phase;    // current stage and the parity of its next fill
   uint32_t slot;            // units consumed in the current stage
   uint32_t c_left;          // units not yet consumed
+  // copy cursor: next unit to copy, units left in its segment, segments
+  // entered, units of the sequence not yet copied
+  const uint8_t* src;
+  uint32_t seg_left, si, cp_left;
+  const Seq* seq;           // this warp's work sequence (shared memory)
 
-  __device__ void setup(uint8_t* smem, uint32_t nst_, int c, uint32_t total) {
+  // Issues the first min(nst, groups) groups (all lanes call).
+  __device__ void setup(uint8_t* smem, uint32_t nst_, int c, uint32_t total, const Seq* seq_, uint32_t* status) {
     nst = nst_;
     ring_saddr = smem_u32(RingShape<UPS>::ring(smem, nst, c));
-    full = RingShape<UPS>::full(smem, nst, c);
-    empty = RingShape<UPS>::empty(smem, nst, c);
+    full_saddr = smem_u32(RingShape<UPS>::full(smem, nst, c));
     stage = phase = slot = 0;
     c_left = total;
+    seq = seq_;
+    src = nullptr;
+    seg_left = si = 0;
+    cp_left = total;
+    for (uint32_t s = 0; s < nst; ++s) refill(s, status);
+  }
+  // Copy the next group (min(UPS, units left)) into stage s: one bulk copy
+  // per segment piece, each inside its segment by construction.  The stage's
+  // previous contents were loaded into registers and consumed by the warp's
+  // earlier instructions, so the copy cannot overwrite data still needed.
+  __device__ __forceinline__ void refill(uint32_t s, uint32_t* status) {
+    const uint32_t n = cp_left < UPS ? cp_left : UPS;
+    if (n == 0) return;
+    const bool l0 = (threadIdx.x & 31) == 0;
+    const uint32_t dst = ring_saddr + s * kStageBytes, bar = full_saddr + s * 8;
+    const uint64_t policy = l2_policy_evict_first();
+    cp_left -= n;
+    if (seg_left >= n) {  // common case: one piece
+      lane0_arm_and_copy(l0, bar, n * kUnitBytes, dst, src, n * kUnitBytes, policy);
+      src += static_cast<size_t>(n) * kUnitBytes;
+      seg_left -= n;
+      return;
+    }
+    const Cursor c = refill_pieces(Cursor{src, seg_left, si}, seq, dst, bar, n, l0, policy, status);
+    src = c.src;
+    seg_left = c.seg_left;
+    si = c.si;
   }
   __device__ __forceinline__ bool wait_full() {  // warp-uniform result
-    return __all_sync(0xffffffffu, mbar_wait_bounded(&full[stage], phase)) != 0;
+    return __all_sync(0xffffffffu, mbar_wait_bounded_s(full_saddr + stage * 8, phase)) != 0;
   }
   __device__ __forceinline__ uint32_t unit_saddr() const {
     return ring_saddr + stage * kStageBytes + slot * kUnitBytes;
@@ -231,15 +367,14 @@ struct ConsumerRing {
     const uint32_t at_start = c_left + slot;
     return (at_start < UPS ? at_start : UPS) - slot;
   }
-  // Consume n units of the current stage; hand a finished stage back.  The
-  // stage's data has been read into registers and used, so the producer may
-  // overwrite it (reads need no proxy fence).
-  __device__ __forceinline__ void consume(uint32_t n, int lane) {
+  // Consume n units of the current stage; refill a finished stage with the
+  // group nst groups ahead.
+  __device__ __forceinline__ void consume(uint32_t n, uint32_t* status) {
     c_left -= n;
     slot += n;
     if (slot == UPS || c_left == 0) {
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[stage]);
+      refill(stage, status);
       slot = 0;
       if (++stage == nst) {
         stage = 0;
@@ -247,101 +382,17 @@ struct ConsumerRing {
       }
     }
   }
-  // Error path: keep the protocol moving without computing, so the producer
-  // can finish and no copy is left in flight; stop if a copy never lands.
-  __device__ void drain(int lane) {
+  // Error path: keep the protocol moving without computing, so no copy is
+  // left in flight; stop if a copy never lands.
+  __device__ void drain(uint32_t* status) {
     while (c_left) {
       if (slot == 0 && !wait_full()) return;
-      consume(stage_left(), lane);
+      consume(stage_left(), status);
     }
   }
 };
 
-// Producer warp: lane c < kConsumerWarps feeds consumer warp c.  Non-blocking round
-// robin: a lane issues its next group when the target stage is empty; the
-// warp sleeps briefly when no lane made progress.  A lane that sees no
-// progress for kWaitTimeoutNs records a timeout and stops.
-template <int UPS>
-__device__ void produce(uint8_t* smem, uint32_t nst, const WorkList& wl, uint64_t policy, uint32_t* status) {
-  constexpr uint32_t kStageBytes = UPS * kUnitBytes;
-  const int lane = threadIdx.x & 31;
-  const bool mine = lane < kConsumerWarps;
-  uint8_t* ring = mine ? RingShape<UPS>::ring(smem, nst, lane) : nullptr;
-  uint64_t* full = mine ? RingShape<UPS>::full(smem, nst, lane) : nullptr;
-  uint64_t* empty = mine ? RingShape<UPS>::empty(smem, nst, lane) : nullptr;
-  const uint8_t* seg0_end = wl.s0 + static_cast<size_t>(wl.c0) * kUnitBytes;
-  const uint8_t* seg1_end = wl.s1 + static_cast<size_t>(wl.c1) * kUnitBytes;
-  const uint8_t* src = wl.c0 ? wl.s0 : wl.s1;
-  uint32_t left0 = wl.c0;
-  uint32_t left = mine ? wl.c0 + wl.c1 : 0;
-  uint32_t g = 0, pstage = 0, round = 0;  // group, its stage, and g / nst
-  unsigned long long last = globaltimer_ns();
-  while (__any_sync(0xffffffffu, left != 0)) {
-    bool progress = false;
-    if (left) {
-      const bool ready = round == 0 || mbar_try_wait(&empty[pstage], (round - 1) & 1);
-      if (ready) {
-        const uint32_t n = left < UPS ? left : UPS;
-        uint8_t* dst = ring + pstage * kStageBytes;
-        bool ok;
-        if (n <= left0 || left0 == 0) {
-          ok = src + static_cast<size_t>(n) * kUnitBytes <= (left0 ? seg0_end : seg1_end);
-          if (ok) {
-            mbar_arrive_expect_tx(&full[pstage], n * kUnitBytes);
-            bulk_g2s(dst, src, n * kUnitBytes, &full[pstage], policy);
-          }
-        } else {  // the group straddles the end of segment 0
-          ok = src + static_cast<size_t>(left0) * kUnitBytes <= seg0_end &&
-               wl.s1 + static_cast<size_t>(n - left0) * kUnitBytes <= seg1_end;
-          if (ok) {
-            mbar_arrive_expect_tx(&full[pstage], n * kUnitBytes);
-            bulk_g2s(dst, src, left0 * kUnitBytes, &full[pstage], policy);
-            bulk_g2s(dst + left0 * kUnitBytes, wl.s1, (n - left0) * kUnitBytes, &full[pstage], policy);
-          }
-        }
-        if (!ok) {  // a copy would leave its segment: report, stop this lane
-          atomicOr(status, kStatusBadLaunch);
-          left = 0;
-        } else {
-          if (n < left0) {
-            src += static_cast<size_t>(n) * kUnitBytes;
-            left0 -= n;
-          } else if (left0 > 0) {
-            src = wl.s1 + static_cast<size_t>(n - left0) * kUnitBytes;
-            left0 = 0;
-          } else {
-            src += static_cast<size_t>(n) * kUnitBytes;
-          }
-          left -= n;
-          ++g;
-          if (++pstage == nst) {
-            pstage = 0;
-            ++round;
-          }
-          progress = true;
-          last = globaltimer_ns();
-        }
-      } else if (globaltimer_ns() - last > kWaitTimeoutNs) {
-        atomicOr(status, kStatusMbarTimeout);
-        left = 0;
-      }
-    }
-    if (!__any_sync(0xffffffffu, progress)) __nanosleep(128);
-  }
-}
-
-// Barrier 2 (all 16 warps): the producer waits there until the consumers have
-// staged their activations, so those few latency-critical loads are not
-// queued behind the weight stream.
-__device__ __forceinline__ void producer_wait_release() {
-  asm volatile("bar.sync 2, %0;" ::"n"((kConsumerWarps + 1) * 32) : "memory");
-}
-__device__ __forceinline__ void consumers_release_producer() {
-  asm volatile("bar.arrive 2, %0;" ::"n"((kConsumerWarps + 1) * 32) : "memory");
-}
-
-// Named barrier and AND-reduction over the consumer warps only (the producer
-// warp runs free).
+// Named barrier and AND-reduction over the CTA's warps (barrier 1).
 __device__ __forceinline__ void consumers_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
 }
@@ -380,12 +431,15 @@ struct UnitMath {
     for (int b = 0; b < 2; ++b)
 #pragma unroll
       for (int h = 0; h < 2; ++h) C[b][h] = FAST ? bf2_mul(S[b][h], kNeg8Sub) : 0u;
+    uint32_t S16[2];  // row g+8 scales times 2^-4 (the nibbles at bits 4-7)
+#pragma unroll
+    for (int b = 0; b < 2; ++b) S16[b] = FAST ? bf2_mul(S[b][1], kPow2m4) : 0u;
     const uint32_t words[4] = {nib.x, nib.y, nib.z, nib.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int b = j >> 1;
       uint32_t a[4];
-      dequant_word<FAST>(words[j], S[b][0], C[b][0], S[b][1], C[b][1], a);
+      dequant_word<FAST>(words[j], S[b][0], C[b][0], S[b][1], C[b][1], S16[b], a);
 #pragma unroll
       for (int grp = 0; grp < NGRP; ++grp) {
         const uint4& v = xf[grp][j >> 1];
@@ -421,6 +475,14 @@ struct UnitMath {
   }
 };
 
+// Units per straight-line run in the consumer's inner loop (a divisor of the
+// stage size): longer runs interleave more independent work, shorter ones
+// keep the loop's instructions resident in the instruction cache.
+#ifndef ALV_STAGE_UNROLL
+#define ALV_STAGE_UNROLL ALV_UNITS_PER_STAGE
+#endif
+constexpr int kStageUnroll = ALV_STAGE_UNROLL;
+
 // Straight-line run of units S..UPS-1 of a full stage.
 template <int NCOLS, bool FAST, int S, int UPS>
 struct StageUnroll {
@@ -436,14 +498,22 @@ struct StageUnroll<NCOLS, FAST, UPS, UPS> {
 };
 
 // ---------------------------------------------------------------------------
-// Split-K fixup scratch.  A row tile covered by several warps is reduced by
-// the last contributor (acq_rel arrival counter) summing every contributor's
-// partial in warp order, so results are deterministic for a given grid.
+// Split-K scratch.  A row tile split between warps of one CTA is reduced in
+// shared memory once the CTA's warps are done (warp partials summed in warp
+// order); a row tile split between CTAs is then finished by the last CTA to
+// arrive (acq_rel arrival counter), CTA partials summed in CTA order.  Fixed
+// orders: results are deterministic for a given grid.
 // ---------------------------------------------------------------------------
 struct Fixup {
-  float* ws;          // [Wtot][2 slots][ntok][16]
-  uint32_t* cnt;      // [RT] arrival counters, zero between launches
+  float* ws;          // global: [nctas][2 slots][ntok][16] CTA partials
+  uint32_t* cnt;      // global: [RT] arrival counters, zero between launches
+  float* part;        // shared: [warps][2 slots][ntok][16] warp partials
 };
+
+// Shared-memory bytes of the warp partials.
+__host__ __device__ constexpr size_t part_bytes(int ntok) {
+  return static_cast<size_t>(kConsumerWarps) * 2 * ntok * 16 * sizeof(float);
+}
 
 __device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
   uint32_t old;
@@ -483,13 +553,12 @@ struct LaneVals {
 };
 
 // ---------------------------------------------------------------------------
-// Finish a row tile: apply epi directly when this warp covered the whole tile,
-// else publish the partial and let the last contributor reduce in warp order.
+// Finish a row tile: apply epi directly when this warp covered the whole
+// tile, else park the partial for cta_fixup.
 // ---------------------------------------------------------------------------
 template <int NCOLS, bool SPLIT, class Epi>
 __device__ __forceinline__ void flush_tile(const float (&acc)[(NCOLS > 8 ? 2 : 1)][2][4], bool whole, uint32_t r,
-                                        uint32_t first_row, uint32_t KT, uint64_t U, uint32_t W,
-                                        const Fixup& fx, uint32_t gw, int ntok, const Epi& epi) {
+                                        uint32_t first_row, const Fixup& fx, int ntok, const Epi& epi) {
   using LV = LaneVals<NCOLS, SPLIT>;
   const int lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
   LV lv;
@@ -502,11 +571,10 @@ __device__ __forceinline__ void flush_tile(const float (&acc)[(NCOLS > 8 ? 2 : 1
     }
     return;
   }
-  const uint32_t w_lo = warp_of_unit(static_cast<uint64_t>(r) * KT, U, W);
-  const uint32_t w_hi = warp_of_unit((static_cast<uint64_t>(r) + 1) * KT - 1, U, W);
+  // Partial row tile: park it in this warp's shared slot (0: the range's
+  // first row, 1: its last row); cta_fixup reduces it after the phase.
   const int slotw = (r == first_row) ? 0 : 1;
-  const size_t slot_floats = static_cast<size_t>(ntok) * 16;
-  float* mine = fx.ws + (static_cast<size_t>(gw) * 2 + slotw) * slot_floats;
+  float* mine = fx.part + (static_cast<size_t>(threadIdx.x >> 5) * 2 + slotw) * ntok * 16;
 #pragma unroll
   for (int i = 0; i < LV::T; ++i) {
     const int tok = LV::tok_of(i, t4);
@@ -515,65 +583,90 @@ __device__ __forceinline__ void flush_tile(const float (&acc)[(NCOLS > 8 ? 2 : 1
       mine[tok * 16 + g + 8] = lv.vg8[i];
     }
   }
-  __syncwarp();
-  uint32_t old = 0;
-  if (lane == 0) old = atom_add_acq_rel_gpu(&fx.cnt[r], 1u);
-  old = __shfl_sync(0xffffffffu, old, 0);
-  if (old != w_hi - w_lo) return;
-  // Gather the contributors' partials CB at a time (independent loads in
-  // flight), then add them in warp order.
-  constexpr int CB = 16 / LV::T;
-  float sg[LV::T], sg8[LV::T];
-#pragma unroll
-  for (int i = 0; i < LV::T; ++i) sg[i] = sg8[i] = 0.f;
-  for (uint32_t w0 = w_lo; w0 <= w_hi; w0 += CB) {
-    float pg[CB][LV::T], pg8[CB][LV::T];
-#pragma unroll
-    for (int c = 0; c < CB; ++c) {
-      const uint32_t w = w0 + c;
-      if (w > w_hi) continue;
-      const uint32_t wfirst = static_cast<uint32_t>(range_start(w, U, W) / KT);
-      const int ws = (r == wfirst) ? 0 : 1;
-      const float* src = fx.ws + (static_cast<size_t>(w) * 2 + ws) * slot_floats;
-#pragma unroll
-      for (int i = 0; i < LV::T; ++i) {
-        const int tok = LV::tok_of(i, t4);
-        pg[c][i] = tok < ntok ? __ldcg(src + tok * 16 + g) : 0.f;
-        pg8[c][i] = tok < ntok ? __ldcg(src + tok * 16 + g + 8) : 0.f;
+}
+
+// ---------------------------------------------------------------------------
+// After every warp of the CTA finished its range: reduce the row tiles that
+// were split between warps (shared memory, warp order) and apply epi to the
+// ones inside the CTA's range; publish CTA partials of the (at most two) row
+// tiles shared with other CTAs and let the last CTA to arrive finish them.
+// All warps of the CTA call this (it syncs them).
+// ---------------------------------------------------------------------------
+template <class Epi>
+__device__ void cta_fixup(const Q4Mat& m, uint64_t W, const Fixup& fx, int ntok, const Epi& epi) {
+  consumers_sync();  // every warp's partials are in shared memory
+  const uint32_t KT = m.KT;
+  const uint64_t U = static_cast<uint64_t>(m.RT) * KT;
+  const uint64_t gw0 = static_cast<uint64_t>(blockIdx.x) * kWarpsPerCtaS;
+  if (gw0 >= W) return;
+  const uint64_t gw1 = gw0 + kWarpsPerCtaS < W ? gw0 + kWarpsPerCtaS : W;
+  const uint64_t c0 = range_start(gw0, U, W), c1 = range_start(gw1, U, W);
+  const uint32_t r_lo = static_cast<uint32_t>(c0 / KT), r_hi = static_cast<uint32_t>((c1 - 1) / KT);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const size_t slot_floats = static_cast<size_t>(ntok) * 16;
+  for (uint32_t r = r_lo + warp; r <= r_hi; r += kWarpsPerCtaS) {
+    const uint64_t rb = static_cast<uint64_t>(r) * KT, re = rb + KT;
+    const bool inside = rb >= c0 && re <= c1;
+    const uint32_t w_lo = warp_of_unit(rb > c0 ? rb : c0, U, W) - static_cast<uint32_t>(gw0);
+    const uint32_t w_hi = warp_of_unit((re < c1 ? re : c1) - 1, U, W) - static_cast<uint32_t>(gw0);
+    if (inside && w_lo == w_hi) continue;  // one warp held the whole tile: applied already
+    const int cslot = (r == r_lo) ? 0 : 1;
+    float* cpart = fx.ws + (static_cast<size_t>(blockIdx.x) * 2 + cslot) * slot_floats;
+    for (uint32_t e = lane; e < 8u * ntok; e += 32) {
+      const int g = e & 7, tok = e >> 3;
+      float vg = 0.f, vg8 = 0.f;
+      for (uint32_t w = w_lo; w <= w_hi; ++w) {
+        const uint32_t wfirst = static_cast<uint32_t>(range_start(gw0 + w, U, W) / KT);
+        const float* src = fx.part + (static_cast<size_t>(w) * 2 + (r == wfirst ? 0 : 1)) * slot_floats;
+        vg += src[tok * 16 + g];
+        vg8 += src[tok * 16 + g + 8];
+      }
+      if (inside) {
+        epi.apply(r, g, tok, vg, vg8);
+      } else {
+        cpart[tok * 16 + g] = vg;
+        cpart[tok * 16 + g + 8] = vg8;
       }
     }
-#pragma unroll
-    for (int c = 0; c < CB; ++c) {
-      if (w0 + c > w_hi) continue;
-#pragma unroll
-      for (int i = 0; i < LV::T; ++i) {
-        sg[i] += pg[c][i];
-        sg8[i] += pg8[c][i];
+    if (inside) continue;
+    // Shared with other CTAs: publish, count, and the last CTA finishes.
+    __threadfence();
+    __syncwarp();
+    uint32_t old = 0;
+    if (lane == 0) old = atom_add_acq_rel_gpu(&fx.cnt[r], 1u);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    const uint32_t cta_lo = warp_of_unit(rb, U, W) / kWarpsPerCtaS;
+    const uint32_t cta_hi = warp_of_unit(re - 1, U, W) / kWarpsPerCtaS;
+    if (old != cta_hi - cta_lo) continue;
+    __threadfence();  // every lane reads the other CTAs' partials after the count
+    for (uint32_t e = lane; e < 8u * ntok; e += 32) {
+      const int g = e & 7, tok = e >> 3;
+      float vg = 0.f, vg8 = 0.f;
+      for (uint32_t c = cta_lo; c <= cta_hi; ++c) {
+        const uint32_t cfirst =
+            static_cast<uint32_t>(range_start(static_cast<uint64_t>(c) * kWarpsPerCtaS, U, W) / KT);
+        const float* src = fx.ws + (static_cast<size_t>(c) * 2 + (r == cfirst ? 0 : 1)) * slot_floats;
+        vg += __ldcg(src + tok * 16 + g);
+        vg8 += __ldcg(src + tok * 16 + g + 8);
       }
+      epi.apply(r, g, tok, vg, vg8);
     }
+    if (lane == 0) fx.cnt[r] = 0;
   }
-#pragma unroll
-  for (int i = 0; i < LV::T; ++i) {
-    const int tok = LV::tok_of(i, t4);
-    if (tok < ntok) epi.apply(r, g, tok, sg[i], sg8[i]);
-  }
-  if (lane == 0) fx.cnt[r] = 0;
 }
 
 // ---------------------------------------------------------------------------
 // Consume the unit range [u0, u1) of matrix m from the warp's ring, applying
-// epi to every finished row tile.  Returns false on a timed-out copy (after
-// draining the ring).  W = participating warps for this matrix.
+// epi to every row tile the warp holds whole and parking the partial ones for
+// cta_fixup.  Returns false on a timed-out copy.
 // ---------------------------------------------------------------------------
-template <int NCOLS, bool SPLIT, bool FAST, int UPS, class Epi>
-__device__ bool consume_range(ConsumerRing<UPS>& ring, const Q4Mat& m, uint32_t u0, uint32_t u1,
-                              const uint8_t* xs, const Fixup& fx, uint32_t gw, uint32_t W, int ntok,
-                              const Epi& epi, uint32_t* status) {
+template <int NCOLS, bool SPLIT, bool FAST, int UPS, class Seq, class Epi>
+__device__ bool consume_range(ConsumerRing<UPS, Seq>& ring, const Q4Mat& m, uint32_t u0, uint32_t u1,
+                              const uint8_t* xs, const Fixup& fx, int ntok, const Epi& epi, uint32_t* status) {
   constexpr int NGRP = NCOLS > 8 ? 2 : 1;
   if (u0 >= u1) return true;
   const int lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
   const uint32_t KT = m.KT;
-  const uint64_t U = static_cast<uint64_t>(m.RT) * KT;
   const uint32_t n_lane = NCOLS >= 8 ? g : (g & (NCOLS - 1));
   const uint8_t* xl = xs + (n_lane * 4 + t4) * 32;
   const uint32_t x_saddr = smem_u32(xl);
@@ -598,22 +691,28 @@ __device__ bool consume_range(ConsumerRing<UPS>& ring, const Q4Mat& m, uint32_t 
     const uint32_t take = sl < left ? sl : left;
     const uint32_t su = ring.unit_saddr();
     if (take == UPS && kt + UPS < KT) {
-      // Common case: a full stage inside one row tile -- straight-line code so
-      // the UPS units' dequant and MMA chains interleave; all shared-memory
-      // offsets are immediates.
-      StageUnroll<NCOLS, FAST, 0, UPS>::go(su + lane * 16, su + kUnitNibBytes + g * 8,
-                                           x_saddr + kt * UnitMath<NCOLS, FAST>::kXStride, acc);
+      // Common case: a full stage inside one row tile -- straight-line runs of
+      // kStageUnroll units so their dequant and MMA chains interleave, with
+      // immediate shared-memory offsets inside a run.
+#pragma unroll 1
+      for (uint32_t q = 0; q < UPS; q += kStageUnroll) {
+        const uint32_t uq = su + q * kUnitBytes;
+        StageUnroll<NCOLS, FAST, 0, kStageUnroll>::go(uq + lane * 16, uq + kUnitNibBytes + g * 8,
+                                                      x_saddr + (kt + q) * UnitMath<NCOLS, FAST>::kXStride, acc);
+      }
       kt += UPS;
-      ring.consume(take, lane);
+      ring.consume(take, status);
       left -= take;
       continue;
     }
-#pragma unroll
-    for (int s = 0; s < UPS; ++s) {
-      if (static_cast<uint32_t>(s) < take) {
+    // Stage that crosses a row-tile end (or a short one): one unit at a time,
+    // kept rolled so the fixup code exists once in the instruction stream.
+#pragma unroll 1
+    for (uint32_t s = 0; s < UPS; ++s) {
+      if (s < take) {
         UnitMath<NCOLS, FAST>::run_saddr(su + s * kUnitBytes, x_saddr, kt, lane, acc);
         if (++kt == KT) {
-          flush_tile<NCOLS, SPLIT>(acc, seg_kt0 == 0, r, first_row, KT, U, W, fx, gw, ntok, epi);
+          flush_tile<NCOLS, SPLIT>(acc, seg_kt0 == 0, r, first_row, fx, ntok, epi);
 #pragma unroll
           for (int a = 0; a < NGRP; ++a)
 #pragma unroll
@@ -625,10 +724,10 @@ __device__ bool consume_range(ConsumerRing<UPS>& ring, const Q4Mat& m, uint32_t 
         }
       }
     }
-    ring.consume(take, lane);
+    ring.consume(take, status);
     left -= take;
   }
-  if (kt != seg_kt0) flush_tile<NCOLS, SPLIT>(acc, false, r, first_row, KT, U, W, fx, gw, ntok, epi);
+  if (kt != seg_kt0) flush_tile<NCOLS, SPLIT>(acc, false, r, first_row, fx, ntok, epi);
   return true;
 }
 

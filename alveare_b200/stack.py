@@ -9,8 +9,10 @@ Tensor parallelism splits each FFN's intermediate dimension over the ranks
 (the reference's I-split across AIE cores, kernels/ffn_fused/ffn_fused.py:46-60,
 lifted to GPUs); the per-layer partial down projections are summed with one
 NCCL all-reduce of H fp32 values (the reference's host partial sum,
-runtime/cpp/src/npu.cpp:360-377).  A step is captured once into a CUDA graph
-and replayed.
+runtime/cpp/src/npu.cpp:360-377).  On one GPU the whole step is a single
+persistent kernel (alv_ffn_stack_run) that streams every layer's weights back
+to back; with tensor parallelism each layer is one kernel followed by the
+all-reduce.  A step is captured once into a CUDA graph and replayed.
 """
 from __future__ import annotations
 
@@ -45,9 +47,13 @@ class FFNStack:
     """
 
     def __init__(self, H: int, I: int, device: int = 0, rank: int = 0, world: int = 1,
-                 activation: str = "gelu"):
+                 activation: str = "gelu", fused: bool = True):
         self.H, self.I, self.device, self.rank, self.world = H, I, device, rank, world
         self.activation = activation
+        # one launch per step (single GPU only: the per-layer all-reduce of
+        # tensor parallelism runs between layer kernels)
+        self.fused = fused and world == 1
+        self.stack_handle = 0
         self.i_begin, self.i_end = tp_slice(I, rank, world)
         self.layers: list[FusedFFNWeight] = []
         dev = torch.device("cuda", device)
@@ -62,8 +68,21 @@ class FFNStack:
         return _lib.context(self.device)
 
     def add_layer(self, gate, up, down) -> None:
+        if self.stack_handle:
+            raise RuntimeError("FFNStack: layers cannot be added after the first step")
         self.layers.append(FusedFFNWeight(gate, up, down, self.H, self.I, self.activation, device=self.device,
                                           i_begin=self.i_begin, i_end=self.i_end))
+
+    def _stack(self) -> int:
+        """Handle of the one-launch stack (created on first use)."""
+        if not self.stack_handle:
+            ctx = self.ctx
+            n = len(self.layers)
+            arr = (ctypes.c_uint32 * n)(*[w.handle for w in self.layers])
+            h = ctypes.c_uint32()
+            ctx.check(ctx.lib.alv_ffn_stack_create(ctx.ptr, arr, n, ctypes.byref(h)), "alv_ffn_stack_create")
+            self.stack_handle = h.value
+        return self.stack_handle
 
     def weight_bytes(self) -> int:
         """Algorithmic weight bytes of the whole stack (all ranks): 18 B per 32 weights."""
@@ -74,6 +93,10 @@ class FFNStack:
         """Enqueue one step on the current stream; returns kernels launched."""
         ctx = self.ctx
         st = torch.cuda.current_stream(self.device).cuda_stream
+        if self.fused:
+            ctx.check(ctx.lib.alv_ffn_stack_run(ctx.ptr, self._stack(), 1, self.x[0].data_ptr(),
+                                                self.out.data_ptr(), st), "alv_ffn_stack_run")
+            return 1
         n = 0
         L = len(self.layers)
         for l, w in enumerate(self.layers):
@@ -122,3 +145,14 @@ class FFNStack:
     def release(self) -> None:
         """Drop captured graphs (before destroying a process group)."""
         self.graph = None
+
+    def free(self) -> None:
+        """Release the stack handle and the layers' device memory."""
+        self.graph = None
+        ctx = self.ctx
+        if self.stack_handle:
+            ctx.check(ctx.lib.alv_weight_destroy(ctx.ptr, self.stack_handle), "alv_weight_destroy")
+            self.stack_handle = 0
+        for w in self.layers:
+            w.free()
+        self.layers = []

@@ -143,6 +143,22 @@ int alv_ffn_layer(alv_ctx* ctx, alv_handle h, int ntok, const uint16_t* x_in,
 int alv_ffn_stack_finalize(alv_ctx* ctx, int ntok, int H, const uint16_t* x_in,
                            const float* down_in, uint16_t* x_out, void* stream);
 
+/* Whole FFN stack of a decode step in one launch: the per-layer loop of the
+ * decode step (runtime/cpp/src/model.cpp:404 inside the layer loop,
+ * runtime/py/model.py:782-806) over n FFN weights, i.e. alv_ffn_layer for
+ * layer 0..n-1 followed by alv_ffn_stack_finalize, with identical results.
+ * The layers must share H, I, activation and dequant path and hold the whole
+ * intermediate dimension (i_begin = 0, i_end = I); the stack references them
+ * (destroy the stack with alv_weight_destroy before its layers).  It owns its
+ * workspace, so a captured launch stays valid.  No counterpart handle exists
+ * in the reference (its registry runs one FFN call per layer). */
+int alv_ffn_stack_create(alv_ctx* ctx, const alv_handle* layers, int n, alv_handle* out);
+
+/* out = stack(x_in): x_in, out bf16 (ntok, H) device buffers, 1 <= ntok <= 4
+ * (ALV_ERR_UNSUPPORTED when the activations do not fit in shared memory). */
+int alv_ffn_stack_run(alv_ctx* ctx, alv_handle stack, int ntok, const uint16_t* x_in, uint16_t* out,
+                      void* stream);
+
 /* Allocation-free gemv: same arithmetic and arguments as alv_gemv, for
  * callers that must not allocate device memory while they run (a decode
  * loop with a fixed GPU memory budget, a host runtime that owns the device
@@ -164,10 +180,10 @@ int alv_gemv_noalloc(alv_ctx* ctx, alv_handle h, int ntok, const void* x, int x_
  * is a device buffer of (#SMs x 16) uint64, every later alv_ffn / alv_ffn_layer
  * launch writes per-CTA %globaltimer stamps (ns): [0] start, [1] input staged,
  * [2] gate/up phase done, [3] grid barrier passed, [4] act staged, [5] down
- * phase done; with the layer glue also [6] inputs landed, [7] glue done,
- * [8]/[9] post-norm reduction / residual done, [10]/[11] pre-norm reduction
- * entered / left.  Slots [12]-[15] are unused.  NULL turns tracing off (the
- * default). */
+ * phase done; with the layer glue also [6] inputs landed, [7] glue done.
+ * alv_ffn_stack_run writes the same stamps for its second layer ([0] glue
+ * start, [1]-[5] as above, [6] the layer's last barrier passed).  Slots
+ * [8]-[15] are unused.  NULL turns tracing off (the default). */
 int alv_set_trace(alv_ctx* ctx, uint64_t* trace);
 
 /* ---- host-buffer convenience (synchronous, like NpuRegistry::run_gemv) ---- */

@@ -219,13 +219,14 @@ def rmsnorm_gemma(x_bf: np.ndarray, w: np.ndarray | None = None, eps: float = 1e
     return to_bf16(normed)
 
 
-def ffn_block_gemma4(x_bf: np.ndarray, gate_c, up_c, down_c, deq=None) -> np.ndarray:
+def ffn_block_gemma4(x_bf: np.ndarray, gate_c, up_c, down_c, deq=None, activation: str = "gelu") -> np.ndarray:
     """One FFN half-block of a Gemma-4 decode layer with unit norm weights.
     Restates runtime/py/model.py:782-810 minus the layer output scale:
     ``x2 = rmsnorm(x)``; ``down = bf16(FFN_geglu(x2))``; ``x + bf16(rmsnorm(down))``
-    with a bf16 residual add."""
+    with a bf16 residual add.  ``activation="silu"`` swaps in the SwiGLU FFN
+    (model.py:854-860) inside the same block, for kernel checks."""
     x2 = rmsnorm_gemma(x_bf)
-    y, _, _, _ = ffn(gate_c, up_c, down_c, x2, "gelu", deq=deq)
+    y, _, _, _ = ffn(gate_c, up_c, down_c, x2, activation, deq=deq)
     down = to_bf16(y)
     down_normed = rmsnorm_gemma(down)
     return to_bf16(np.asarray(x_bf, dtype=np.float32) + down_normed)

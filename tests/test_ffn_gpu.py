@@ -144,8 +144,10 @@ def test_ffn_layer_stack_matches_oracle():
                                              final.data_ptr(), st), "finalize")
     ctx.sync_status()
     got = q4.bits_to_f32(final.cpu().numpy().view(np.uint16))
-    assert normwise(got, ref) <= 1e-2  # bf16 residual stream: 3 chained roundings
-    assert np.mean(got == ref) > 0.95
+    # bf16 residual stream: a bf16 rounding flipped by a different fp32 sum
+    # order propagates down the chain, so only a normwise bound holds here
+    # (layer-by-layer parity: tests/test_stack_gpu.py)
+    assert normwise(got, ref) <= 1e-2
 
 
 def test_ffn_generic_dequant_path_shared_by_both_matrices():
