@@ -55,6 +55,7 @@ SIGNATURES = {
     "alv_run_gemv": (_i, [_vp, _u32, _i, _vp, _i, _vp, _i]),
     "alv_run_ffn": (_i, [_vp, _u32, _i, _vp, _i, _vp, _i]),
     "alv_gemv_noalloc": (_i, [_vp, _u32, _i, _vp, _i, _vp, _i, _vp]),
+    "alv_gemm": (_i, [_vp, _u32, _i, _vp, _vp, _i, _vp]),
     "alv_set_trace": (_i, [_vp, _vp]),
 }
 

@@ -272,14 +272,57 @@ def gemv_q_npu(W_combined, X, Y, *, N: int, K: int, m: int = 32, k_tile: int = 2
             w.free()
 
 
+# Batches above this many bf16 tokens run on the tcgen05 prefill kernel; the
+# decode-sized ones stay on the HBM-bound streaming gemv.
+GEMM_TC_MIN_TOKENS = 17
+
+
+def _gemm_tc(w, B: int, Xv, Yv) -> None:
+    """Y = X W^T through alv_gemm (bf16 X on the device, 16-byte aligned)."""
+    ctx, device = w.ctx, w.device
+    yd = _dtype_code(Yv)
+    if _is_torch(Xv) and Xv.is_cuda:
+        xt = Xv.contiguous()
+    else:
+        xt = torch.from_numpy(np.ascontiguousarray(_host_array(Xv)).view(np.int16)).to(
+            torch.device("cuda", device)).view(torch.bfloat16)
+    if xt.data_ptr() % 16:
+        xt = xt.clone()
+    on_dev = _is_torch(Yv) and Yv.is_cuda
+    if on_dev and Yv.is_contiguous():
+        yt = Yv
+    else:
+        yt = torch.empty((B, Yv.shape[-1]), dtype=torch.float32 if yd == F32 else torch.bfloat16,
+                         device=torch.device("cuda", device))
+    ctx.check(ctx.lib.alv_gemm(ctx.ptr, w.handle, B, xt.data_ptr(), yt.data_ptr(), yd, _stream(device)), "alv_gemm")
+    if yt is not Yv:
+        if on_dev:
+            Yv.copy_(yt)
+        else:
+            torch.cuda.current_stream(device).synchronize()
+            ctx.sync_status(_stream(device))
+            host = yt.cpu()
+            if _is_torch(Yv):
+                Yv.copy_(host)
+            elif yd == F32:
+                Yv[...] = host.numpy()
+            else:
+                Yv[...] = host.view(torch.int16).numpy().view(Yv.dtype)
+
+
 def gemm_q_npu(W_combined, X, Y, *, B: int, N: int, K: int, m: int = 32, k_tile: int = 256) -> None:
     """Y[B, N] = X[B, K] @ W^T for the Q4 matrix W (kernels/gemm_q/gemm_q.py:28-39).
-    Batches larger than 16 are processed in slices of 16 tokens."""
+    bf16 batches of GEMM_TC_MIN_TOKENS or more run on the tensor cores
+    (tcgen05); smaller ones (and fp32 X) are processed by the streaming gemv
+    in slices of 16 (8 for fp32) tokens."""
     device = _device_of(X, Y, W_combined)
     w, temp = _as_weight(W_combined, N, K, device)
     try:
         Xv = X.reshape(B, K) if not (len(X.shape) == 2 and tuple(X.shape) == (B, K)) else X
         Yv = Y.reshape(B, N) if not (len(Y.shape) == 2 and tuple(Y.shape) == (B, N)) else Y
+        if _dtype_code(X) == BF16 and B >= GEMM_TC_MIN_TOKENS:
+            _gemm_tc(w, B, Xv, Yv)
+            return
         step = 16 if _dtype_code(X) == BF16 else 8
         for b0 in range(0, B, step):
             b1 = min(B, b0 + step)

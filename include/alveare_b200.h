@@ -121,6 +121,15 @@ int alv_weight_dequantize(alv_ctx* ctx, alv_handle h, int which, uint16_t* out, 
 int alv_gemv(alv_ctx* ctx, alv_handle h, int ntok, const void* x, int x_dtype, void* y,
              int y_dtype, void* stream);
 
+/* Batched prefill on the tensor cores: Y[b, n] = sum_k X[b, k] * W[n, k] for
+ * b < B (any B >= 1), X bf16 (B, K) row-major on the device, 16-byte aligned;
+ * Y (B, N) fp32 or bf16; fp32 accumulation.  The Q4 weight is dequantized to
+ * bf16 in shared memory tile by tile and multiplied with tcgen05.mma (the
+ * accumulator lives in tensor memory).  Replaces NpuRegistry::run_gemm /
+ * run_gemm_streamed (npu.cpp:291-338) and the gemm_q NPU design
+ * (kernels/gemm_q/gemm_q.py:28-143, gemm_q.cc:18-54). */
+int alv_gemm(alv_ctx* ctx, alv_handle h, int B, const uint16_t* x, void* y, int y_dtype, void* stream);
+
 /* Fused FFN on the registered slice: gate = bf16(Wg x), up = bf16(Wu x),
  * act = bf16(act_fn(gate) * up), y = Wd act (fp32 accumulate).  x is
  * (ntok, H), y is (ntok, H); 1 <= ntok <= 8.  For a tensor-parallel slice y
