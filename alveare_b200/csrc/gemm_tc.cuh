@@ -8,14 +8,15 @@
 // check is X_f32 @ dequantize_combined(W).astype(f32).T (gemm_q.py:185-188).
 //
 // One CTA computes a 128-weight-row x NT-token tile, stepping K by 64:
-//   warp 4      copies the stage's eight Q4 units (1-D bulk copies) and the X
+//   warp 8      copies the stage's eight Q4 units (1-D bulk copies) and the X
 //               tile (2-D tensor copy, 128-byte swizzle, no multicast)
-//   warps 0-3   dequantize the units straight into the A buffer in the
+//   warps 0-7   dequantize one unit each straight into the A buffer in the
 //               K-major 128-byte-swizzle layout the tensor core reads
-//   warp 5      one thread issues tcgen05.mma (M=128, N=NT, K=16) x 4 and
+//   warp 9      one thread issues tcgen05.mma (M=128, N=NT, K=16) x 4 and
 //               commits to the stage's `empty` barrier
-// then warps 0-3 read the accumulator back with tcgen05.ld (warp w owns TMEM
-// lanes 32w..32w+31, i.e. weight rows) and store Y.  Every wait gives up
+// then warps 0-7 read the accumulator back with tcgen05.ld (warp w owns TMEM
+// lanes 32(w%4)..+31, i.e. weight rows, and half of the token columns) and
+// store Y.  Every wait gives up
 // after 1 s (status bit; the CTA stops consuming, lets its copies land and
 // frees its tensor memory before returning).
 #pragma once
@@ -26,8 +27,9 @@
 namespace alv {
 
 constexpr int kTcM = 128;        // weight rows per tile: 8 unit rows of 16
-constexpr int kTcStages = 3;
-constexpr int kTcThreads = 192;  // 4 dequant/epilogue warps, 1 copy warp, 1 MMA warp
+constexpr int kTcStages = 4;
+constexpr int kTcDeqWarps = 8;   // one unit (16 weight rows) each per stage
+constexpr int kTcThreads = (kTcDeqWarps + 2) * 32;  // + 1 copy warp + 1 MMA warp
 
 struct GemmParams {
   Q4Mat m;           // weight units; m.RT*16 >= N rows, m.KT*64 >= K
@@ -132,7 +134,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTcStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&deq[s], 4);
+      mbar_init(&deq[s], kTcDeqWarps);
       mbar_init(&empty[s], 1);
     }
     mbar_init(&accb, 1);
@@ -150,7 +152,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
 
-  if (warp == 4) {
+  if (warp == kTcDeqWarps) {
     // ---- copies ----
     if (lane == 0) {
       uint32_t armed = 0;  // stages armed so far
@@ -175,7 +177,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
       for (uint32_t kc = armed > kTcStages ? armed - kTcStages : 0; kc < armed; ++kc)
         mbar_wait_bounded(&full[kc % kTcStages], (kc / kTcStages) & 1);
     }
-  } else if (warp == 5) {
+  } else if (warp == kTcDeqWarps + 1) {
     // ---- tensor-core issue ----
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_bf16_f32(kTcM, NT);
@@ -197,7 +199,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
       umma_commit(smem_u32(&accb));  // completes once every issued MMA is done
     }
   } else {
-    // ---- dequant (warps 0-3: units 2w, 2w+1 of each stage) ----
+    // ---- dequant (warp w: unit w of each stage) ----
     const int g = lane >> 2, t4 = lane & 3;
     for (uint32_t kc = 0; kc < KC && !failed; ++kc) {
       const uint32_t s = kc % kTcStages, ph = (kc / kTcStages) & 1;
@@ -207,9 +209,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
         break;
       }
       const uint32_t st = base + s * Lay::kStage;
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint32_t u = 2 * warp + h;
+      {
+        const uint32_t u = warp;
         uint32_t a[4][4];
         if (u < nrt) {
           const uint32_t ua = st + Lay::kA + Lay::kX + u * kUnitBytes;
@@ -255,12 +256,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     const bool acc_ok = mbar_wait_bounded(&accb, 0);
     tc_fence_after();
     if (acc_ok && !failed) {
-      const uint32_t row = blockIdx.x * kTcM + warp * 32 + lane;
+      const uint32_t quad = warp & 3, half = warp >> 2;
+      const uint32_t row = blockIdx.x * kTcM + quad * 32 + lane;
       const float sm = p.m.scale_mul;
 #pragma unroll 1
-      for (uint32_t c = 0; c < static_cast<uint32_t>(NT); c += 16) {
+      for (uint32_t c = half * (NT / 2); c < (half + 1) * (NT / 2); c += 16) {
         float v[16];
-        tmem_ld16(tmem + (static_cast<uint32_t>(warp * 32) << 16) + c, v);
+        tmem_ld16(tmem + ((quad * 32) << 16) + c, v);
         if (row < p.N) {
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
