@@ -434,17 +434,19 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) gemv_kernel(const GemvParam
     u0 = static_cast<uint32_t>(range_start(gw, U, W));
     u1 = static_cast<uint32_t>(range_start(gw + 1, U, W));
   }
-  if (lane == 0) wl[warp] = WorkList{p.m.units + static_cast<size_t>(u0) * kUnitBytes, p.m.units, u1 - u0, 0};
+  if (lane == 0)
+    wl[warp] = WorkList{p.m.units + static_cast<size_t>(u0) * kUnitBytes, p.m.units, u1 - u0, 0,
+                        u0 % p.m.KT, 0, p.m.KT, 1};
   __syncthreads();
   ConsumerRing<kUnitsPerStage, WorkList> ring;
-  ring.setup(smem, p.nst, warp, u1 - u0, &wl[warp], p.status);  // weights start streaming
+  ring.setup(smem, p.nst, warp, u1 - u0, &wl[warp]);  // weights start streaming
   Fixup fx = p.fx;
   fx.part = reinterpret_cast<float*>(smem + ring_smem_bytes(p.nst));
   uint8_t* xs = smem + base_smem_bytes(p.nst, p.x.ntok);
   stage_frags<NCOLS, SPLIT>(xs, p.m.KT, p.x);
   consumers_sync();
   if (!consume_range<NCOLS, SPLIT, FAST>(ring, p.m, u0, u1, xs, fx, p.x.ntok, p.epi, p.status))
-    ring.drain(p.status);
+    ring.drain();
   cta_fixup(p.m, W, fx, p.x.ntok, p.epi);
 }
 
@@ -603,7 +605,8 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_kernel(const FfnParams 
   }
   if (lane == 0)
     wl[warp] = WorkList{p.gu.units + static_cast<size_t>(a0) * kUnitBytes,
-                        p.dn.units + static_cast<size_t>(b0) * kUnitBytes, a1 - a0, b1 - b0};
+                        p.dn.units + static_cast<size_t>(b0) * kUnitBytes, a1 - a0, b1 - b0,
+                        a0 % p.gu.KT, b0 % p.dn.KT, p.gu.KT, p.dn.KT};
   // Shared layout after the rings and warp partials:
   // [xs frags][red][tmp ntok*H f32][x_in raw][down_in raw][xbar]
   Fixup fxA = p.fxA, fxB = p.fxB;
@@ -633,7 +636,7 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_kernel(const FfnParams 
     if (db) bulk_g2s(draw, p.down_in, db, xbar, pol);
   }
   ConsumerRing<kUnitsPerStage, WorkList> ring;
-  ring.setup(smem, p.nst, warp, (a1 - a0) + (b1 - b0), &wl[warp], p.status);
+  ring.setup(smem, p.nst, warp, (a1 - a0) + (b1 - b0), &wl[warp]);
   trace_mark(p.trace, 0);
 
   // The act padding (k in [I, 64*dn.KT)) must read as zero in phase B.
@@ -673,7 +676,7 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_kernel(const FfnParams 
   const bool bar_ok = grid_barrier(p.bar, gridDim.x, p.status);
   trace_mark(p.trace, 3);
   if (!bar_ok || !consumers_and(ok)) {
-    ring.drain(p.status);
+    ring.drain();
     return;
   }
   // act is already in fragment order: stage it with 16-byte copies through L2.
@@ -682,7 +685,7 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_kernel(const FfnParams 
   consumers_sync();
   trace_mark(p.trace, 4);
   if (!consume_range<NCB, false, FAST>(ring, p.dn, b0, b1, xs, fxB, p.ntok, p.out, p.status))
-    ring.drain(p.status);
+    ring.drain();
   cta_fixup(p.dn, WB, fxB, p.ntok, p.out);
   if (p.trace) {
     consumers_sync();
@@ -780,12 +783,12 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const Stac
     uint32_t* w = wk[warp];
     w[0] = a0; w[1] = a1; w[2] = b0; w[3] = b1;
     w[4] = gw; w[5] = static_cast<uint32_t>(WA); w[6] = static_cast<uint32_t>(WB);
-    sw[warp] = StackWork{p.layers, p.L, a0, a1 - a0, b0, b1 - b0};
+    sw[warp] = StackWork{p.layers, p.L, a0, a1 - a0, b0, b1 - b0, p.gu.KT, p.dn.KT};
   }
   __syncthreads();
   const uint32_t* my = wk[warp];
   ConsumerRing<kUnitsPerStage, StackWork> ring;
-  ring.setup(smem, p.nst, warp, p.L * ((my[1] - my[0]) + (my[3] - my[2])), &sw[warp], p.status);
+  ring.setup(smem, p.nst, warp, p.L * ((my[1] - my[0]) + (my[3] - my[2])), &sw[warp]);
   // The act padding (k in [I, 64*dn.KT)) must read as zero in phase B.
   if (blockIdx.x == 0) {
     const uint32_t kpad = p.dn.KT * 64;
@@ -828,7 +831,7 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const Stac
       trace_mark(tr, B ? 5 : 2);
     }
     if (!grid_barrier(p.bar, gridDim.x, p.status) || !consumers_and(ok)) {
-      ring.drain(p.status);
+      ring.drain();
       return;
     }
     trace_mark(tr, B ? 6 : 3);

@@ -189,15 +189,23 @@ __host__ __device__ constexpr size_t frag_bytes(uint32_t KT, int ncols) {
 // concatenated sequence, so a stage may span segment ends.
 // ---------------------------------------------------------------------------
 
+// A warp's work is a sequence of segments: contiguous unit ranges of one
+// matrix.  get(i, ...) gives segment i's first unit, its length, the matrix's
+// k tiles per row tile (KT) and the k tile the segment starts at.
+
 // Work of one warp as two segments (segment 0 then segment 1).
 struct WorkList {
   const uint8_t* s0;   // first unit of segment 0
   const uint8_t* s1;   // first unit of segment 1
   uint32_t c0, c1;     // units in each segment
+  uint32_t kt0, kt1;   // k tile of each segment's first unit
+  uint32_t KT0, KT1;   // k tiles per row tile of each segment's matrix
   __device__ uint32_t nseg() const { return 2; }
-  __device__ void get(uint32_t i, const uint8_t*& base, uint32_t& n) const {
+  __device__ void get(uint32_t i, const uint8_t*& base, uint32_t& n, uint32_t& KT, uint32_t& kt) const {
     base = i ? s1 : s0;
     n = i ? c1 : c0;
+    KT = i ? KT1 : KT0;
+    kt = i ? kt1 : kt0;
   }
 };
 
@@ -214,17 +222,22 @@ struct LayerW {
 struct StackWork {
   const LayerW* layers;
   uint32_t L, a0, na, b0, nb;
+  uint32_t KTA, KTB;   // k tiles per row tile of gate/up and of down
   __device__ uint32_t nseg() const { return 2 * L; }
-  __device__ void get(uint32_t i, const uint8_t*& base, uint32_t& n) const {
+  __device__ void get(uint32_t i, const uint8_t*& base, uint32_t& n, uint32_t& KT, uint32_t& kt) const {
     const LayerW* lw = layers + (i >> 1);
     if (i & 1) {
       base = reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(&lw->dn))) +
              static_cast<size_t>(b0) * kUnitBytes;
       n = nb;
+      KT = KTB;
+      kt = b0 % KTB;
     } else {
       base = reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(&lw->gu))) +
              static_cast<size_t>(a0) * kUnitBytes;
       n = na;
+      KT = KTA;
+      kt = a0 % KTA;
     }
   }
 };
@@ -251,60 +264,47 @@ struct RingShape {
   }
 };
 
-// Lane 0 only (pred): arm `bar` for `bytes` and start one bulk copy into it.
+// Lane 0 only (pred): arm `bar` for `bytes` and start one bulk copy of them.
 __device__ __forceinline__ void lane0_arm_and_copy(bool pred, uint32_t bar, uint32_t bytes, uint32_t dst,
-                                                   const void* src, uint32_t copy_bytes, uint64_t policy) {
+                                                   const void* src, uint64_t policy) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.u32 p, %0, 0;\n\t"
       "@p mbarrier.arrive.expect_tx.shared::cta.b64 _, [%1], %2;\n\t"
       "@p cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%3], [%4], %5, [%1], %6;\n\t}" ::"r"(static_cast<uint32_t>(pred)),
-      "r"(bar), "r"(bytes), "r"(dst), "l"(src), "r"(copy_bytes), "l"(policy)
-      : "memory");
-}
-__device__ __forceinline__ void lane0_copy(bool pred, uint32_t bar, uint32_t dst, const void* src,
-                                           uint32_t copy_bytes, uint64_t policy) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.u32 p, %0, 0;\n\t"
-      "@p cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%2], [%3], %4, [%1], %5;\n\t}" ::"r"(static_cast<uint32_t>(pred)),
-      "r"(bar), "r"(dst), "l"(src), "r"(copy_bytes), "l"(policy)
+      " [%3], [%4], %2, [%1], %5;\n\t}" ::"r"(static_cast<uint32_t>(pred)),
+      "r"(bar), "r"(bytes), "r"(dst), "l"(src), "l"(policy)
       : "memory");
 }
 
-// Copy cursor state passed by value to the out-of-line multi-piece refill.
+// Copy cursor: position in the warp's segment sequence.
 struct Cursor {
-  const uint8_t* src;
-  uint32_t seg_left, si;
+  const uint8_t* src;   // next unit to copy
+  uint32_t seg_left;    // units of the current segment not yet copied
+  uint32_t row_left;    // units until the current row tile ends
+  uint32_t KT;          // k tiles per row tile of the current segment
+  uint32_t si;          // segments entered so far
 };
 
-// Rare path of a refill: the group spans segment ends (or starts the
-// sequence).  Arms `bar` for n units and copies them piece by piece, each
-// piece inside its segment by construction.
+// Rare path of a refill: step to the next non-empty segment.
 template <class Seq>
-__device__ __noinline__ Cursor refill_pieces(Cursor c, const Seq* seq, uint32_t dst, uint32_t bar, uint32_t n,
-                                             bool l0, uint64_t policy, uint32_t* status) {
-  if (l0) mbar_arrive_expect_tx_s(bar, n * kUnitBytes);
+__device__ __noinline__ Cursor next_segment(Cursor c, const Seq* seq) {
   const Seq sq = *seq;
   const uint32_t nseg = sq.nseg();
-  uint32_t k = 0;
-  while (k < n) {
-    while (c.seg_left == 0 && c.si < nseg) sq.get(c.si++, c.src, c.seg_left);
-    if (c.seg_left == 0) break;  // cannot happen: n <= units left in the sequence
-    const uint32_t m = (n - k) < c.seg_left ? (n - k) : c.seg_left;
-    lane0_copy(l0, bar, dst + k * kUnitBytes, c.src, m * kUnitBytes, policy);
-    c.src += static_cast<size_t>(m) * kUnitBytes;
-    c.seg_left -= m;
-    k += m;
+  while (c.seg_left == 0 && c.si < nseg) {
+    uint32_t kt;
+    sq.get(c.si++, c.src, c.seg_left, c.KT, kt);
+    c.row_left = c.KT - kt;
   }
-  if (k != n && l0) atomicOr(status, kStatusBadLaunch);  // the stage's wait will time out
   return c;
 }
 
-// One warp's ring.  The copy cursor lives in registers and is updated by all
-// lanes alike (uniform control flow); lane 0 alone issues the copies.
+// One warp's ring.  Groups are cut at segment and row-tile ends, so a stage
+// always holds units of one row tile of one matrix: min(UPS, units to the
+// row tile's end, units left in the segment).  The consumer derives the same
+// size from its own position.  The copy cursor lives in registers and is
+// advanced by all lanes alike (uniform control flow); lane 0 alone issues the
+// copies.
 template <int UPS, class Seq>
 struct ConsumerRing {
   static constexpr uint32_t kStageBytes = UPS * kUnitBytes;
@@ -312,82 +312,64 @@ struct ConsumerRing {
   uint32_t full_saddr;      // shared address of this warp's full[0]
   uint32_t nst;
   uint32_t stage, phase;    // current stage and the parity of its next fill
-  uint32_t slot;            // units consumed in the current stage
-  uint32_t c_left;          // units not yet consumed
-  // copy cursor: next unit to copy, units left in its segment, segments
-  // entered, units of the sequence not yet copied
-  const uint8_t* src;
-  uint32_t seg_left, si, cp_left;
+  uint32_t inflight;        // groups copied and not yet released
+  uint32_t cp_left;         // units of the sequence not yet copied
+  Cursor cur;
   const Seq* seq;           // this warp's work sequence (shared memory)
 
-  // Issues the first min(nst, groups) groups (all lanes call).
-  __device__ void setup(uint8_t* smem, uint32_t nst_, int c, uint32_t total, const Seq* seq_, uint32_t* status) {
+  // total = units of the whole sequence.  Issues the first groups (all lanes call).
+  __device__ void setup(uint8_t* smem, uint32_t nst_, int c, uint32_t total, const Seq* seq_) {
     nst = nst_;
     ring_saddr = smem_u32(RingShape<UPS>::ring(smem, nst, c));
     full_saddr = smem_u32(RingShape<UPS>::full(smem, nst, c));
-    stage = phase = slot = 0;
-    c_left = total;
-    seq = seq_;
-    src = nullptr;
-    seg_left = si = 0;
+    stage = phase = inflight = 0;
     cp_left = total;
-    for (uint32_t s = 0; s < nst; ++s) refill(s, status);
+    cur = Cursor{nullptr, 0, 0, 1, 0};
+    seq = seq_;
+    for (uint32_t s = 0; s < nst; ++s) refill(s);
   }
-  // Copy the next group (min(UPS, units left)) into stage s: one bulk copy
-  // per segment piece, each inside its segment by construction.  The stage's
+  // Copy the next group into stage s (a single bulk copy).  The stage's
   // previous contents were loaded into registers and consumed by the warp's
   // earlier instructions, so the copy cannot overwrite data still needed.
-  __device__ __forceinline__ void refill(uint32_t s, uint32_t* status) {
-    const uint32_t n = cp_left < UPS ? cp_left : UPS;
-    if (n == 0) return;
-    const bool l0 = (threadIdx.x & 31) == 0;
-    const uint32_t dst = ring_saddr + s * kStageBytes, bar = full_saddr + s * 8;
-    const uint64_t policy = l2_policy_evict_first();
+  __device__ __forceinline__ void refill(uint32_t s) {
+    if (cp_left == 0) return;
+    if (cur.seg_left == 0) cur = next_segment(cur, seq);
+    uint32_t n = cur.seg_left < cur.row_left ? cur.seg_left : cur.row_left;
+    if (n > UPS) n = UPS;
+    if (n == 0) return;  // cannot happen (cp_left counts the segments); the wait for it times out
+    lane0_arm_and_copy((threadIdx.x & 31) == 0, full_saddr + s * 8, n * kUnitBytes, ring_saddr + s * kStageBytes,
+                       cur.src, l2_policy_evict_first());
+    cur.src += static_cast<size_t>(n) * kUnitBytes;
+    cur.seg_left -= n;
+    cur.row_left -= n;
+    if (cur.row_left == 0) cur.row_left = cur.KT;
     cp_left -= n;
-    if (seg_left >= n) {  // common case: one piece
-      lane0_arm_and_copy(l0, bar, n * kUnitBytes, dst, src, n * kUnitBytes, policy);
-      src += static_cast<size_t>(n) * kUnitBytes;
-      seg_left -= n;
-      return;
-    }
-    const Cursor c = refill_pieces(Cursor{src, seg_left, si}, seq, dst, bar, n, l0, policy, status);
-    src = c.src;
-    seg_left = c.seg_left;
-    si = c.si;
+    ++inflight;
   }
   __device__ __forceinline__ bool wait_full() {  // warp-uniform result
     return __all_sync(0xffffffffu, mbar_wait_bounded_s(full_saddr + stage * 8, phase)) != 0;
   }
-  __device__ __forceinline__ uint32_t unit_saddr() const {
-    return ring_saddr + stage * kStageBytes + slot * kUnitBytes;
+  __device__ __forceinline__ uint32_t stage_saddr() const { return ring_saddr + stage * kStageBytes; }
+  // The current stage has been used: refill it with the group nst ahead and
+  // move on.
+  __device__ __forceinline__ void release() {
+    __syncwarp();
+    --inflight;
+    refill(stage);
+    if (++stage == nst) {
+      stage = 0;
+      phase ^= 1;
+    }
   }
-  // Units left in the current stage (its group holds min(UPS, units left at
-  // the group's start) units).
-  __device__ __forceinline__ uint32_t stage_left() const {
-    const uint32_t at_start = c_left + slot;
-    return (at_start < UPS ? at_start : UPS) - slot;
-  }
-  // Consume n units of the current stage; refill a finished stage with the
-  // group nst groups ahead.
-  __device__ __forceinline__ void consume(uint32_t n, uint32_t* status) {
-    c_left -= n;
-    slot += n;
-    if (slot == UPS || c_left == 0) {
-      __syncwarp();
-      refill(stage, status);
-      slot = 0;
+  // Error path: let every copy in flight land (bounded), issue no more.
+  __device__ void drain() {
+    while (inflight) {
+      if (!wait_full()) return;
+      --inflight;
       if (++stage == nst) {
         stage = 0;
         phase ^= 1;
       }
-    }
-  }
-  // Error path: keep the protocol moving without computing, so no copy is
-  // left in flight; stop if a copy never lands.
-  __device__ void drain(uint32_t* status) {
-    while (c_left) {
-      if (slot == 0 && !wait_full()) return;
-      consume(stage_left(), status);
     }
   }
 };
@@ -668,8 +650,7 @@ __device__ bool consume_range(ConsumerRing<UPS, Seq>& ring, const Q4Mat& m, uint
   const int lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
   const uint32_t KT = m.KT;
   const uint32_t n_lane = NCOLS >= 8 ? g : (g & (NCOLS - 1));
-  const uint8_t* xl = xs + (n_lane * 4 + t4) * 32;
-  const uint32_t x_saddr = smem_u32(xl);
+  const uint32_t x_saddr = smem_u32(xs + (n_lane * 4 + t4) * 32);
   const uint32_t first_row = u0 / KT;
   uint32_t r = first_row;
   uint32_t kt = u0 - r * KT;
@@ -683,49 +664,44 @@ __device__ bool consume_range(ConsumerRing<UPS, Seq>& ring, const Q4Mat& m, uint
 #pragma unroll
       for (int c = 0; c < 4; ++c) acc[a][b][c] = 0.f;
   while (left) {
-    if (ring.slot == 0 && !ring.wait_full()) {
+    if (!ring.wait_full()) {
       if (lane == 0) atomicOr(status, kStatusMbarTimeout);
       return false;
     }
-    const uint32_t sl = ring.stage_left();
-    const uint32_t take = sl < left ? sl : left;
-    const uint32_t su = ring.unit_saddr();
-    if (take == UPS && kt + UPS < KT) {
-      // Common case: a full stage inside one row tile -- straight-line runs of
-      // kStageUnroll units so their dequant and MMA chains interleave, with
-      // immediate shared-memory offsets inside a run.
+    const uint32_t su = ring.stage_saddr();
+    // This stage's group: the units up to the row tile's end, at most UPS.
+    uint32_t n = KT - kt;
+    if (n > UPS) n = UPS;
+    if (n > left) n = left;
+    if (n == UPS) {
+      // Common case: a full stage -- straight-line runs of kStageUnroll units
+      // so their dequant and MMA chains interleave, with immediate
+      // shared-memory offsets inside a run.
 #pragma unroll 1
       for (uint32_t q = 0; q < UPS; q += kStageUnroll) {
         const uint32_t uq = su + q * kUnitBytes;
         StageUnroll<NCOLS, FAST, 0, kStageUnroll>::go(uq + lane * 16, uq + kUnitNibBytes + g * 8,
                                                       x_saddr + (kt + q) * UnitMath<NCOLS, FAST>::kXStride, acc);
       }
-      kt += UPS;
-      ring.consume(take, status);
-      left -= take;
-      continue;
-    }
-    // Stage that crosses a row-tile end (or a short one): one unit at a time,
-    // kept rolled so the fixup code exists once in the instruction stream.
+    } else {
 #pragma unroll 1
-    for (uint32_t s = 0; s < UPS; ++s) {
-      if (s < take) {
-        UnitMath<NCOLS, FAST>::run_saddr(su + s * kUnitBytes, x_saddr, kt, lane, acc);
-        if (++kt == KT) {
-          flush_tile<NCOLS, SPLIT>(acc, seg_kt0 == 0, r, first_row, fx, ntok, epi);
-#pragma unroll
-          for (int a = 0; a < NGRP; ++a)
-#pragma unroll
-            for (int b = 0; b < 2; ++b)
-#pragma unroll
-              for (int c = 0; c < 4; ++c) acc[a][b][c] = 0.f;
-          ++r;
-          kt = seg_kt0 = 0;
-        }
-      }
+      for (uint32_t s = 0; s < n; ++s)
+        UnitMath<NCOLS, FAST>::run_saddr(su + s * kUnitBytes, x_saddr, kt + s, lane, acc);
     }
-    ring.consume(take, status);
-    left -= take;
+    ring.release();
+    kt += n;
+    left -= n;
+    if (kt == KT) {
+      flush_tile<NCOLS, SPLIT>(acc, seg_kt0 == 0, r, first_row, fx, ntok, epi);
+#pragma unroll
+      for (int a = 0; a < NGRP; ++a)
+#pragma unroll
+        for (int b = 0; b < 2; ++b)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) acc[a][b][c] = 0.f;
+      ++r;
+      kt = seg_kt0 = 0;
+    }
   }
   if (kt != seg_kt0) flush_tile<NCOLS, SPLIT>(acc, false, r, first_row, fx, ntok, epi);
   return true;
