@@ -931,10 +931,11 @@ StackLayout stack_layout(alv_ctx* ctx, const Weight* w) {
 
 template <int NT, bool FAST>
 int launch_stack_t(alv_ctx* ctx, StackParams p, cudaStream_t st) {
-  const size_t other = stack_smem_bytes(0, p.gu.KT, p.dn.KT, NT, p.H, p.ntok);
+  const uint32_t nctas = static_cast<uint32_t>(ctx->num_sms);
+  const size_t other = stack_smem_bytes(0, p.gu.KT, p.dn.KT, NT, p.H, p.ntok, p.dn.RT, nctas);
   p.nst = ring_stages(other);
   if (!p.nst) return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn_stack: H, I or ntok too large for shared memory");
-  const size_t smem = stack_smem_bytes(p.nst, p.gu.KT, p.dn.KT, NT, p.H, p.ntok);
+  const size_t smem = stack_smem_bytes(p.nst, p.gu.KT, p.dn.KT, NT, p.H, p.ntok, p.dn.RT, nctas);
   auto k = ffn_stack_kernel<NT, FAST>;
   int rc = prepare_kernel(ctx, k, smem);
   if (rc) return rc;

@@ -424,19 +424,19 @@ template <int NCOLS, bool SPLIT, bool FAST>
 __global__ void __launch_bounds__(kThreadsPerCta, 1) gemv_kernel(const GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ WorkList wl[kConsumerWarps];
+  __shared__ uint32_t wr[kConsumerWarps][4];  // per warp: unit range [u0, u1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint64_t U = static_cast<uint64_t>(p.m.RT) * p.m.KT;
-  const uint64_t W = effective_warps(static_cast<uint64_t>(gridDim.x) * kWarpsPerCta, U, p.m.KT);
+  const Partition pt = Partition::make(p.m.RT, p.m.KT, gridDim.x);
   Shape::init_barriers(smem, p.nst);
-  const uint32_t gw = participant_index(blockIdx.x, static_cast<uint32_t>(warp));
-  uint32_t u0 = 0, u1 = 0;
-  if (gw < W) {
-    u0 = static_cast<uint32_t>(range_start(gw, U, W));
-    u1 = static_cast<uint32_t>(range_start(gw + 1, U, W));
-  }
-  if (lane == 0)
+  uint64_t w0, w1;
+  pt.warp_range(blockIdx.x, warp, w0, w1);
+  const uint32_t u0 = static_cast<uint32_t>(w0), u1 = static_cast<uint32_t>(w1);
+  if (lane == 0) {
     wl[warp] = WorkList{p.m.units + static_cast<size_t>(u0) * kUnitBytes, p.m.units, u1 - u0, 0,
                         u0 % p.m.KT, 0, p.m.KT, 1};
+    wr[warp][0] = u0;
+    wr[warp][1] = u1;
+  }
   __syncthreads();
   ConsumerRing<kUnitsPerStage, WorkList> ring;
   ring.setup(smem, p.nst, warp, u1 - u0, &wl[warp]);  // weights start streaming
@@ -447,7 +447,7 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) gemv_kernel(const GemvParam
   consumers_sync();
   if (!consume_range<NCOLS, SPLIT, FAST>(ring, p.m, u0, u1, xs, fx, p.x.ntok, p.epi, p.status))
     ring.drain();
-  cta_fixup(p.m, W, fx, p.x.ntok, p.epi);
+  cta_fixup(pt, &wr[0][0], fx, p.x.ntok, p.epi);
 }
 
 // ===========================================================================
@@ -498,20 +498,70 @@ __device__ __forceinline__ void trace_mark(unsigned long long* trace, int i) {
 // ---------------------------------------------------------------------------
 constexpr int kGlueRegs = 16;
 
+// Loaders: value of token tok at index h, flat index i = tok * H + h.
 struct Bf16In {   // bf16 values in memory written before the launch (or shared)
   const uint16_t* p;
-  __device__ __forceinline__ float operator()(size_t i) const { return bf16_bits_to_f32(p[i]); }
+  __device__ __forceinline__ float operator()(uint32_t, uint32_t, size_t i) const { return bf16_bits_to_f32(p[i]); }
 };
 struct F32In {    // fp32 values in memory written before the launch (or shared)
   const float* p;
-  __device__ __forceinline__ float operator()(size_t i) const { return p[i]; }
+  __device__ __forceinline__ float operator()(uint32_t, uint32_t, size_t i) const { return p[i]; }
+  __device__ __forceinline__ void load(uint32_t, uint32_t, size_t i, float& a, float& b, uint32_t& how) const {
+    a = p[i];
+    b = 0.f;
+    how = 0;
+  }
+  __device__ __forceinline__ float combine(float a, float, uint32_t) const { return a; }
 };
-struct F32InL2 {  // fp32 values written earlier in this launch by other CTAs
-  const float* p;
-  __device__ __forceinline__ float operator()(size_t i) const { return __ldcg(p + i); }
+// The down projection of the previous stack layer as the glue reads it
+// (token tok, index h, flat i = tok*H + h): a row tile held by one CTA is
+// final in `down`; a row tile split between CTAs was left as CTA partials
+// (cta_fixup<true>) that are summed here in CTA order and scaled, exactly as
+// the last CTA to arrive would have done.  split[r] = element offsets in ws
+// of the first two CTAs' partials of row tile r (x = ~0: not split), or
+// y = ~0 with x = the first CTA when the tile spans three or more CTAs.
+struct DownIn {
+  const float* down;
+  const float* ws;          // CTA partials: [CTA][2 slots][ntok][16]
+  const uint2* split;       // per row tile, see above
+  const uint32_t* cfirst;   // per CTA: its first row tile
+  const uint32_t* span;     // per row tile: first CTA | last CTA << 16
+  uint32_t slot_floats;
+  float sm;
+  // Two passes, so a thread's loads are all in flight before any is used:
+  // load() issues them, combine() adds and scales.
+  __device__ __forceinline__ void load(uint32_t tok, uint32_t h, size_t i, float& a, float& b, uint32_t& how) const {
+    const uint32_t r = h >> 4;
+    const uint2 o = split[r];
+    const uint32_t e = tok * 16 + (h & 15);
+    if (o.x == ~0u) {
+      a = __ldcg(down + i);
+      b = 0.f;
+      how = 0;
+    } else if (o.y != ~0u) {
+      a = __ldcg(ws + o.x + e);
+      b = __ldcg(ws + o.y + e);
+      how = 1;
+    } else {  // a row tile over three or more CTAs (small problems)
+      const uint32_t sp = span[r];
+      float v = 0.f;
+      for (uint32_t c = sp & 0xFFFFu; c <= (sp >> 16); ++c)
+        v += __ldcg(ws + (static_cast<size_t>(c) * 2 + (r == cfirst[c] ? 0 : 1)) * slot_floats + e);
+      a = v;
+      b = 0.f;
+      how = 2;
+    }
+  }
+  __device__ __forceinline__ float combine(float a, float b, uint32_t how) const {
+    return how == 0 ? a : (how == 1 ? (a + b) * sm : a * sm);
+  }
 };
 struct NoIn {
-  __device__ __forceinline__ float operator()(size_t) const { return 0.f; }
+  __device__ __forceinline__ void load(uint32_t, uint32_t, size_t, float& a, float& b, uint32_t& how) const {
+    a = b = 0.f;
+    how = 0;
+  }
+  __device__ __forceinline__ float combine(float a, float, uint32_t) const { return a; }
 };
 struct Bf16Out {  // null: no output
   uint16_t* p;
@@ -533,13 +583,20 @@ __device__ void glue_tokens(int ntok, uint32_t H, float eps, const XL& xl, const
   int rs = 0;
   for (int tok = 0; tok < ntok; ++tok) {
     const size_t base = static_cast<size_t>(tok) * H;
-    float xv[GR], dv[GR];
+    // Two passes so every load of the token is in flight before any is used.
+    float xv[GR], dv[GR], db[GR];
+    uint32_t how = 0;  // 2 bits per element
 #pragma unroll
     for (int i = 0; i < GR; ++i) {
       const uint32_t h = threadIdx.x + i * NTHR;
-      xv[i] = h < H ? xl(base + h) : 0.f;
-      dv[i] = (HAS_D && h < H) ? bf16_round(dl(base + h)) : 0.f;
+      xv[i] = h < H ? xl(tok, h, base + h) : 0.f;
+      dv[i] = db[i] = 0.f;
+      uint32_t hw = 0;
+      if (HAS_D && h < H) dl.load(tok, h, base + h, dv[i], db[i], hw);
+      how |= hw << (2 * i);
     }
+#pragma unroll
+    for (int i = 0; i < GR; ++i) dv[i] = HAS_D ? bf16_round(dl.combine(dv[i], db[i], (how >> (2 * i)) & 3)) : 0.f;
     if (HAS_D) {
       float ss = 0.f;
 #pragma unroll
@@ -587,26 +644,25 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_kernel(const FfnParams 
   constexpr uint32_t NTHR = kConsumerWarps * 32;
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint64_t Wtot = static_cast<uint64_t>(gridDim.x) * kWarpsPerCta;
-  const uint64_t UA = static_cast<uint64_t>(p.gu.RT) * p.gu.KT;
-  const uint64_t UB = static_cast<uint64_t>(p.dn.RT) * p.dn.KT;
-  const uint64_t WA = effective_warps(Wtot, UA, p.gu.KT), WB = effective_warps(Wtot, UB, p.dn.KT);
+  const Partition ptA = Partition::make(p.gu.RT, p.gu.KT, gridDim.x);
+  const Partition ptB = Partition::make(p.dn.RT, p.dn.KT, gridDim.x);
   __shared__ WorkList wl[kConsumerWarps];
+  __shared__ uint32_t wr[kConsumerWarps][4];  // per warp: gate/up [u0, u1), down [u0, u1)
   Shape::init_barriers(smem, p.nst);
-  const uint32_t gw = participant_index(blockIdx.x, static_cast<uint32_t>(warp));
-  uint32_t a0 = 0, a1 = 0, b0 = 0, b1 = 0;
-  if (gw < WA) {
-    a0 = static_cast<uint32_t>(range_start(gw, UA, WA));
-    a1 = static_cast<uint32_t>(range_start(gw + 1, UA, WA));
-  }
-  if (gw < WB) {
-    b0 = static_cast<uint32_t>(range_start(gw, UB, WB));
-    b1 = static_cast<uint32_t>(range_start(gw + 1, UB, WB));
-  }
-  if (lane == 0)
+  uint64_t wa0, wa1, wb0, wb1;
+  ptA.warp_range(blockIdx.x, warp, wa0, wa1);
+  ptB.warp_range(blockIdx.x, warp, wb0, wb1);
+  const uint32_t a0 = static_cast<uint32_t>(wa0), a1 = static_cast<uint32_t>(wa1);
+  const uint32_t b0 = static_cast<uint32_t>(wb0), b1 = static_cast<uint32_t>(wb1);
+  if (lane == 0) {
     wl[warp] = WorkList{p.gu.units + static_cast<size_t>(a0) * kUnitBytes,
                         p.dn.units + static_cast<size_t>(b0) * kUnitBytes, a1 - a0, b1 - b0,
                         a0 % p.gu.KT, b0 % p.dn.KT, p.gu.KT, p.dn.KT};
+    wr[warp][0] = a0;
+    wr[warp][1] = a1;
+    wr[warp][2] = b0;
+    wr[warp][3] = b1;
+  }
   // Shared layout after the rings and warp partials:
   // [xs frags][red][tmp ntok*H f32][x_in raw][down_in raw][xbar]
   Fixup fxA = p.fxA, fxB = p.fxB;
@@ -668,7 +724,7 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_kernel(const FfnParams 
 
   GateUpEpi ge{p.act, p.I, NCB, p.gu.scale_mul, p.fn};
   const bool ok = consume_range<NCA, SPLIT, FAST>(ring, p.gu, a0, a1, xs, fxA, p.ntok, ge, p.status);
-  cta_fixup(p.gu, WA, fxA, p.ntok, ge);
+  cta_fixup(ptA, &wr[0][0], fxA, p.ntok, ge);
   if (p.trace) {
     consumers_sync();
     trace_mark(p.trace, 2);
@@ -686,7 +742,7 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_kernel(const FfnParams 
   trace_mark(p.trace, 4);
   if (!consume_range<NCB, false, FAST>(ring, p.dn, b0, b1, xs, fxB, p.ntok, p.out, p.status))
     ring.drain();
-  cta_fixup(p.dn, WB, fxB, p.ntok, p.out);
+  cta_fixup(ptB, &wr[0][2], fxB, p.ntok, p.out);
   if (p.trace) {
     consumers_sync();
     trace_mark(p.trace, 5);
@@ -751,9 +807,15 @@ __host__ __device__ inline size_t stack_xs_region(uint32_t KTA, uint32_t KTB, in
   const size_t a = frag_bytes(KTA, nc) + static_cast<size_t>(ntok) * H * 4;
   return ((b > a ? b : a) + 15) / 16 * 16;
 }
+// [...][xres][down row splits: dn.RT uint2][row spans: dn.RT u32][CTA first rows: #CTAs u32]
+__host__ __device__ inline size_t stack_tables_offset(uint32_t nst, uint32_t KTA, uint32_t KTB, int nc, uint32_t H,
+                                                      int ntok) {
+  return (base_smem_bytes(nst, ntok) + stack_xs_region(KTA, KTB, nc, H, ntok) + 128 +
+          static_cast<size_t>(ntok) * H * 2 + 15) / 16 * 16;
+}
 __host__ __device__ inline size_t stack_smem_bytes(uint32_t nst, uint32_t KTA, uint32_t KTB, int nc, uint32_t H,
-                                                   int ntok) {
-  return base_smem_bytes(nst, ntok) + stack_xs_region(KTA, KTB, nc, H, ntok) + 128 + static_cast<size_t>(ntok) * H * 2;
+                                                   int ntok, uint32_t RTB, uint32_t nctas) {
+  return stack_tables_offset(nst, KTA, KTB, nc, H, ntok) + (static_cast<size_t>(RTB) * 3 + nctas) * 4;
 }
 
 template <int NT, bool FAST>
@@ -761,34 +823,56 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const Stac
   constexpr int NC = NT;  // bf16 activations: one fragment column per token
   constexpr uint32_t NTHR = kConsumerWarps * 32;
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ uint32_t wk[kConsumerWarps][8];  // per warp: a0 a1 b0 b1 gw WA WB
+  __shared__ uint32_t wk[kConsumerWarps][4];  // per warp: a0 a1 b0 b1
   __shared__ StackWork sw[kConsumerWarps];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const Partition ptA = Partition::make(p.gu.RT, p.gu.KT, gridDim.x);
+  const Partition ptB = Partition::make(p.dn.RT, p.dn.KT, gridDim.x);
   Shape::init_barriers(smem, p.nst);
   if (lane == 0) {
-    const uint64_t Wtot = static_cast<uint64_t>(gridDim.x) * kWarpsPerCta;
-    const uint64_t UA = static_cast<uint64_t>(p.gu.RT) * p.gu.KT;
-    const uint64_t UB = static_cast<uint64_t>(p.dn.RT) * p.dn.KT;
-    const uint64_t WA = effective_warps(Wtot, UA, p.gu.KT), WB = effective_warps(Wtot, UB, p.dn.KT);
-    const uint32_t gw = participant_index(blockIdx.x, static_cast<uint32_t>(warp));
-    uint32_t a0 = 0, a1 = 0, b0 = 0, b1 = 0;
-    if (gw < WA) {
-      a0 = static_cast<uint32_t>(range_start(gw, UA, WA));
-      a1 = static_cast<uint32_t>(range_start(gw + 1, UA, WA));
-    }
-    if (gw < WB) {
-      b0 = static_cast<uint32_t>(range_start(gw, UB, WB));
-      b1 = static_cast<uint32_t>(range_start(gw + 1, UB, WB));
-    }
+    uint64_t a0, a1, b0, b1;
+    ptA.warp_range(blockIdx.x, warp, a0, a1);
+    ptB.warp_range(blockIdx.x, warp, b0, b1);
     uint32_t* w = wk[warp];
-    w[0] = a0; w[1] = a1; w[2] = b0; w[3] = b1;
-    w[4] = gw; w[5] = static_cast<uint32_t>(WA); w[6] = static_cast<uint32_t>(WB);
-    sw[warp] = StackWork{p.layers, p.L, a0, a1 - a0, b0, b1 - b0, p.gu.KT, p.dn.KT};
+    w[0] = static_cast<uint32_t>(a0);
+    w[1] = static_cast<uint32_t>(a1);
+    w[2] = static_cast<uint32_t>(b0);
+    w[3] = static_cast<uint32_t>(b1);
+    sw[warp] = StackWork{p.layers, p.L, w[0], w[1] - w[0], w[2], w[3] - w[2], p.gu.KT, p.dn.KT};
+  }
+  // Down row tiles -> the CTAs holding them (one CTA: `down` has the row;
+  // several: the glue sums their partials), and each CTA's first row tile.
+  uint2* split = reinterpret_cast<uint2*>(smem + stack_tables_offset(p.nst, p.gu.KT, p.dn.KT, NC, p.H, p.ntok));
+  uint32_t* span = reinterpret_cast<uint32_t*>(split + p.dn.RT);
+  uint32_t* cfirst = span + p.dn.RT;
+  for (uint32_t r = threadIdx.x; r < p.dn.RT; r += blockDim.x) {
+    const uint64_t rb = static_cast<uint64_t>(r) * p.dn.KT;
+    span[r] = ptB.aligned ? 0u : (ptB.cta_of_unit(rb) | (ptB.cta_of_unit(rb + p.dn.KT - 1) << 16));
+  }
+  for (uint32_t c = threadIdx.x; c < gridDim.x; c += blockDim.x)
+    cfirst[c] = static_cast<uint32_t>(ptB.cta_begin(c) / p.dn.KT);
+  __syncthreads();
+  for (uint32_t r = threadIdx.x; r < p.dn.RT; r += blockDim.x) {
+    const uint32_t clo = span[r] & 0xFFFFu, chi = span[r] >> 16;
+    const uint32_t sf = static_cast<uint32_t>(p.ntok) * 16;
+    uint2 o = make_uint2(~0u, ~0u);
+    if (chi == clo + 1) {
+      o.x = (clo * 2 + (r == cfirst[clo] ? 0 : 1)) * sf;
+      o.y = (chi * 2 + (r == cfirst[chi] ? 0 : 1)) * sf;
+    } else if (chi > clo + 1) {
+      o.x = clo;
+    }
+    split[r] = o;
   }
   __syncthreads();
   const uint32_t* my = wk[warp];
   ConsumerRing<kUnitsPerStage, StackWork> ring;
   ring.setup(smem, p.nst, warp, p.L * ((my[1] - my[0]) + (my[3] - my[2])), &sw[warp]);
+  // The previous layer's down projection as the glue reads it.
+  auto down_in = [&](uint32_t l) {
+    return DownIn{p.down, p.fxB.ws, split, cfirst, span, static_cast<uint32_t>(p.ntok) * 16,
+                  __ldg(&p.layers[l].dn_mul)};
+  };
   // The act padding (k in [I, 64*dn.KT)) must read as zero in phase B.
   if (blockIdx.x == 0) {
     const uint32_t kpad = p.dn.KT * 64;
@@ -811,7 +895,7 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const Stac
       if (l == 0)
         glue<true, false>(p.ntok, p.H, p.eps, Bf16In{p.x_in}, NoIn{}, Bf16Out{xres}, tmp, red);
       else
-        glue<true, true>(p.ntok, p.H, p.eps, Bf16In{xres}, F32InL2{p.down}, Bf16Out{xres}, tmp, red);
+        glue<true, true>(p.ntok, p.H, p.eps, Bf16In{xres}, down_in(l - 1), Bf16Out{xres}, tmp, red);
       stage_frags<NC, false>(xs, p.gu.KT, SmemSrc{tmp, p.ntok, p.H});
     } else {
       const uint32_t xs_b = static_cast<uint32_t>(frag_bytes(p.dn.KT, NC));
@@ -825,7 +909,14 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const Stac
     fx.part = reinterpret_cast<float*>(smem + ring_smem_bytes(p.nst));
     const bool ok = consume_range<NC, false, FAST>(ring, B ? p.dn : p.gu, my[B ? 2 : 0], my[B ? 3 : 1], xs, fx,
                                                    p.ntok, epi, p.status);
-    cta_fixup(B ? p.dn : p.gu, my[B ? 6 : 5], fx, p.ntok, epi);
+    if (tr) {
+      consumers_sync();
+      trace_mark(tr, B ? 8 : 7);
+    }
+    if (B)
+      cta_fixup<true>(ptB, &wk[0][2], fx, p.ntok, epi);  // rows shared between CTAs: summed by the next glue
+    else
+      cta_fixup(ptA, &wk[0][0], fx, p.ntok, epi);
     if (tr) {
       consumers_sync();
       trace_mark(tr, B ? 5 : 2);
@@ -839,7 +930,7 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const Stac
   if (blockIdx.x == 0) {
     float* red = reinterpret_cast<float*>(smem + base_smem_bytes(p.nst, p.ntok) +
                                           stack_xs_region(p.gu.KT, p.dn.KT, NC, p.H, p.ntok));
-    glue<false, true>(p.ntok, p.H, p.eps, Bf16In{reinterpret_cast<uint16_t*>(red + 32)}, F32InL2{p.down},
+    glue<false, true>(p.ntok, p.H, p.eps, Bf16In{reinterpret_cast<uint16_t*>(red + 32)}, down_in(p.L - 1),
                       Bf16Out{p.out}, nullptr, red);
   }
 }

@@ -61,30 +61,68 @@ struct Q4Mat {
 };
 
 // Contiguous split of U units over W warps: warp w owns [start(w), start(w+1)).
-// W <= U, so every participating warp owns >= 1 unit (the fixup counts
-// contributors as contiguous warp and CTA intervals).
-__device__ __forceinline__ uint64_t range_start(uint64_t w, uint64_t U, uint64_t W) {
+__host__ __device__ __forceinline__ uint64_t range_start(uint64_t w, uint64_t U, uint64_t W) {
   return w * U / W;
 }
 // Participating warps for U units of a matrix with KT k tiles: every warp
-// owns >= 1 unit, and >= ceil(KT/16) units so that no row tile is split over
-// more than ~16 warps (the split-K fixup gathers one partial per contributor).
+// owns >= 1 unit, and >= ceil(KT/16) units.
 __host__ __device__ __forceinline__ uint64_t effective_warps(uint64_t Wtot, uint64_t U, uint64_t KT) {
   const uint64_t min_units = (KT + 15) / 16;
   uint64_t w = U / (min_units ? min_units : 1);
   if (w < 1) w = 1;
   return w < Wtot ? w : Wtot;
 }
-// Participating warp index of warp `warp` of CTA `cta`: CTA-major, so a CTA
-// owns one contiguous unit range and a row tile split between its warps is
-// reduced in shared memory.
-__device__ __forceinline__ uint32_t participant_index(uint32_t cta, uint32_t warp) {
-  return cta * kWarpsPerCtaS + warp;
-}
 // The warp whose range contains unit u.
-__device__ __forceinline__ uint32_t warp_of_unit(uint64_t u, uint64_t U, uint64_t W) {
+__host__ __device__ __forceinline__ uint32_t warp_of_unit(uint64_t u, uint64_t U, uint64_t W) {
   return static_cast<uint32_t>(((u + 1) * W - 1) / U);
 }
+
+// How a matrix's RT x KT units are split over the grid: CTA c owns one
+// contiguous unit range and its warps split that range.  Row-aligned when
+// every CTA can take whole row tiles at < 1/32 imbalance (then no row tile
+// spans two CTAs and the split-K reduction stays in shared memory);
+// otherwise unit-balanced: W participating warps numbered CTA-major, warp gw
+// owning [gw*U/W, (gw+1)*U/W).
+struct Partition {
+  uint64_t U, W;
+  uint32_t RT, KT, nctas, aligned;
+
+  __host__ __device__ static Partition make(uint32_t RT, uint32_t KT, uint32_t nctas) {
+    Partition p;
+    p.RT = RT;
+    p.KT = KT;
+    p.nctas = nctas;
+    p.U = static_cast<uint64_t>(RT) * KT;
+    const uint64_t per = (static_cast<uint64_t>(RT) + nctas - 1) / nctas;
+    p.aligned = RT >= nctas && per * nctas * 32 <= static_cast<uint64_t>(RT) * 33;
+    p.W = effective_warps(static_cast<uint64_t>(nctas) * kWarpsPerCtaS, p.U, KT);
+    return p;
+  }
+  // First unit of CTA c (c = nctas gives U).
+  __host__ __device__ uint64_t cta_begin(uint32_t c) const {
+    if (aligned) return static_cast<uint64_t>(c) * RT / nctas * KT;
+    const uint64_t gw = static_cast<uint64_t>(c) * kWarpsPerCtaS;
+    return range_start(gw < W ? gw : W, U, W);
+  }
+  // Units [u0, u1) of warp w of CTA c (possibly empty).
+  __host__ __device__ void warp_range(uint32_t c, uint32_t w, uint64_t& u0, uint64_t& u1) const {
+    if (aligned) {
+      const uint64_t c0 = cta_begin(c), len = cta_begin(c + 1) - c0;
+      u0 = c0 + len * w / kWarpsPerCtaS;
+      u1 = c0 + len * (w + 1) / kWarpsPerCtaS;
+      return;
+    }
+    const uint64_t gw = static_cast<uint64_t>(c) * kWarpsPerCtaS + w;
+    if (gw >= W) {
+      u0 = u1 = U;
+      return;
+    }
+    u0 = range_start(gw, U, W);
+    u1 = range_start(gw + 1, U, W);
+  }
+  // CTA holding unit u (unit-balanced partitions only).
+  __host__ __device__ uint32_t cta_of_unit(uint64_t u) const { return warp_of_unit(u, U, W) / kWarpsPerCtaS; }
+};
 
 // ---------------------------------------------------------------------------
 // Dequantize one 32-bit nibble word into the four bf16x2 A-fragment registers.
@@ -570,36 +608,47 @@ __device__ __forceinline__ void flush_tile(const float (&acc)[(NCOLS > 8 ? 2 : 1
 // ---------------------------------------------------------------------------
 // After every warp of the CTA finished its range: reduce the row tiles that
 // were split between warps (shared memory, warp order) and apply epi to the
-// ones inside the CTA's range; publish CTA partials of the (at most two) row
-// tiles shared with other CTAs and let the last CTA to arrive finish them.
-// All warps of the CTA call this (it syncs them).
+// ones inside the CTA's range.  Row tiles shared with other CTAs (unit-
+// balanced partitions only) get a CTA partial in fx.ws; unless DEFER, the
+// last CTA to arrive (acq_rel counter) sums them in CTA order and applies
+// epi.  With DEFER the partials are left for the consumer of the result to
+// sum after the next grid barrier (SplitRows).  All warps of the CTA call
+// this (it syncs them).
 // ---------------------------------------------------------------------------
-template <class Epi>
-__device__ void cta_fixup(const Q4Mat& m, uint64_t W, const Fixup& fx, int ntok, const Epi& epi) {
+template <bool DEFER = false, class Epi>
+__device__ void cta_fixup(const Partition& pt, const uint32_t* wr, const Fixup& fx, int ntok, const Epi& epi) {
+  // wr[4 * w + 0 / 1]: unit range [u0, u1) of warp w of this CTA (shared memory)
   consumers_sync();  // every warp's partials are in shared memory
-  const uint32_t KT = m.KT;
-  const uint64_t U = static_cast<uint64_t>(m.RT) * KT;
-  const uint64_t gw0 = static_cast<uint64_t>(blockIdx.x) * kWarpsPerCtaS;
-  if (gw0 >= W) return;
-  const uint64_t gw1 = gw0 + kWarpsPerCtaS < W ? gw0 + kWarpsPerCtaS : W;
-  const uint64_t c0 = range_start(gw0, U, W), c1 = range_start(gw1, U, W);
+  const uint32_t KT = pt.KT, c = blockIdx.x;
+  const uint64_t c0 = pt.cta_begin(c), c1 = pt.cta_begin(c + 1);
+  if (c0 >= c1) return;
   const uint32_t r_lo = static_cast<uint32_t>(c0 / KT), r_hi = static_cast<uint32_t>((c1 - 1) / KT);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const size_t slot_floats = static_cast<size_t>(ntok) * 16;
   for (uint32_t r = r_lo + warp; r <= r_hi; r += kWarpsPerCtaS) {
     const uint64_t rb = static_cast<uint64_t>(r) * KT, re = rb + KT;
+    const uint64_t ib = rb > c0 ? rb : c0, ie = re < c1 ? re : c1;  // this CTA's part of the row tile
     const bool inside = rb >= c0 && re <= c1;
-    const uint32_t w_lo = warp_of_unit(rb > c0 ? rb : c0, U, W) - static_cast<uint32_t>(gw0);
-    const uint32_t w_hi = warp_of_unit((re < c1 ? re : c1) - 1, U, W) - static_cast<uint32_t>(gw0);
-    if (inside && w_lo == w_hi) continue;  // one warp held the whole tile: applied already
+    // Contributing warps (contiguous): ranges that meet [ib, ie).
+    uint32_t w_lo = kWarpsPerCtaS, w_hi = 0;
+    bool whole = false;
+    for (uint32_t w = 0; w < kWarpsPerCtaS; ++w) {
+      const uint32_t u0 = wr[4 * w], u1 = wr[4 * w + 1];
+      if (u0 < ie && u1 > ib) {
+        w_lo = w < w_lo ? w : w_lo;
+        w_hi = w;
+        whole = u0 <= rb && u1 >= re;
+      }
+    }
+    if (w_lo > w_hi) continue;
+    if (inside && w_lo == w_hi && whole) continue;  // one warp held the whole tile: applied already
     const int cslot = (r == r_lo) ? 0 : 1;
-    float* cpart = fx.ws + (static_cast<size_t>(blockIdx.x) * 2 + cslot) * slot_floats;
+    float* cpart = fx.ws + (static_cast<size_t>(c) * 2 + cslot) * slot_floats;
     for (uint32_t e = lane; e < 8u * ntok; e += 32) {
       const int g = e & 7, tok = e >> 3;
       float vg = 0.f, vg8 = 0.f;
       for (uint32_t w = w_lo; w <= w_hi; ++w) {
-        const uint32_t wfirst = static_cast<uint32_t>(range_start(gw0 + w, U, W) / KT);
-        const float* src = fx.part + (static_cast<size_t>(w) * 2 + (r == wfirst ? 0 : 1)) * slot_floats;
+        const float* src = fx.part + (static_cast<size_t>(w) * 2 + (r == wr[4 * w] / KT ? 0 : 1)) * slot_floats;
         vg += src[tok * 16 + g];
         vg8 += src[tok * 16 + g + 8];
       }
@@ -610,24 +659,22 @@ __device__ void cta_fixup(const Q4Mat& m, uint64_t W, const Fixup& fx, int ntok,
         cpart[tok * 16 + g + 8] = vg8;
       }
     }
-    if (inside) continue;
+    if (inside || DEFER) continue;
     // Shared with other CTAs: publish, count, and the last CTA finishes.
     __threadfence();
     __syncwarp();
     uint32_t old = 0;
     if (lane == 0) old = atom_add_acq_rel_gpu(&fx.cnt[r], 1u);
     old = __shfl_sync(0xffffffffu, old, 0);
-    const uint32_t cta_lo = warp_of_unit(rb, U, W) / kWarpsPerCtaS;
-    const uint32_t cta_hi = warp_of_unit(re - 1, U, W) / kWarpsPerCtaS;
+    const uint32_t cta_lo = pt.cta_of_unit(rb), cta_hi = pt.cta_of_unit(re - 1);
     if (old != cta_hi - cta_lo) continue;
     __threadfence();  // every lane reads the other CTAs' partials after the count
     for (uint32_t e = lane; e < 8u * ntok; e += 32) {
       const int g = e & 7, tok = e >> 3;
       float vg = 0.f, vg8 = 0.f;
-      for (uint32_t c = cta_lo; c <= cta_hi; ++c) {
-        const uint32_t cfirst =
-            static_cast<uint32_t>(range_start(static_cast<uint64_t>(c) * kWarpsPerCtaS, U, W) / KT);
-        const float* src = fx.ws + (static_cast<size_t>(c) * 2 + (r == cfirst ? 0 : 1)) * slot_floats;
+      for (uint32_t cc = cta_lo; cc <= cta_hi; ++cc) {
+        const uint32_t cfirst = static_cast<uint32_t>(pt.cta_begin(cc) / KT);
+        const float* src = fx.ws + (static_cast<size_t>(cc) * 2 + (r == cfirst ? 0 : 1)) * slot_floats;
         vg += __ldcg(src + tok * 16 + g);
         vg8 += __ldcg(src + tok * 16 + g + 8);
       }

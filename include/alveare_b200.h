@@ -191,8 +191,9 @@ int alv_gemv_noalloc(alv_ctx* ctx, alv_handle h, int ntok, const void* x, int x_
  * [2] gate/up phase done, [3] grid barrier passed, [4] act staged, [5] down
  * phase done; with the layer glue also [6] inputs landed, [7] glue done.
  * alv_ffn_stack_run writes the same stamps for its second layer ([0] glue
- * start, [1]-[5] as above, [6] the layer's last barrier passed).  Slots
- * [8]-[15] are unused.  NULL turns tracing off (the default). */
+ * start, [1]-[5] as above, [6] the layer's last barrier passed, [7] / [8]
+ * gate/up / down units streamed, before the split-K reduction).  Slots
+ * [9]-[15] are unused.  NULL turns tracing off (the default). */
 int alv_set_trace(alv_ctx* ctx, uint64_t* trace);
 
 /* ---- host-buffer convenience (synchronous, like NpuRegistry::run_gemv) ---- */
