@@ -363,6 +363,43 @@ __device__ bool grid_barrier(GridBar* gb, uint32_t nblocks, uint32_t* status) {
   return consumers_and(ok != 0);
 }
 
+// Grid barrier for a kernel that passes it many times (the FFN stack): the
+// arrival is a fire-and-forget release reduction and the target is known in
+// advance, so a CTA pays one poll round trip, not an atomic's return trip
+// plus the poll.  `base` is the counter's value at launch, read once before
+// the first arrival (grid_base); `epoch` counts this launch's barriers.
+__device__ __forceinline__ unsigned long long grid_base(GridBar* gb, uint32_t nblocks) {
+  // At most nblocks - 1 arrivals of this launch can precede the read (the
+  // first barrier needs every CTA), and launches start at multiples of nblocks.
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(&gb->count) : "memory");
+  return v / nblocks * nblocks;
+}
+__device__ bool grid_barrier_epoch(GridBar* gb, uint32_t nblocks, unsigned long long base, uint32_t epoch,
+                                   uint32_t* status) {
+  consumers_sync();
+  int ok = 1;
+  if (threadIdx.x == 0) {
+    asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(&gb->count) : "memory");
+    const unsigned long long target = base + static_cast<unsigned long long>(epoch) * nblocks;
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(&gb->count) : "memory");
+    if (v < target) {
+      const unsigned long long t0 = globaltimer_ns();
+      while (true) {
+        asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(&gb->count) : "memory");
+        if (v >= target) break;
+        if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+          atomicOr(status, kStatusGridTimeout);
+          ok = 0;
+          break;
+        }
+      }
+    }
+  }
+  return consumers_and(ok != 0);
+}
+
 // Sum over the consumer threads (all of them get the result) through `red`
 // (>= 16 floats).  One named barrier: consecutive calls must alternate
 // between two such buffers (a call's buffer is rewritten two calls later,
@@ -570,10 +607,19 @@ struct Bf16Out {  // null: no output
   }
 };
 
-// xn (PRE) goes to xn_out[ntok][H] (fp32 holding bf16 values).
+// Where xn (PRE) goes: straight into the B-fragment layout of the next
+// phase (frag: nc columns, kpad = 64 * k tiles; every position outside
+// [0, ntok) x [0, H) is zeroed), or as fp32 (holding bf16 values) into
+// tmp[ntok][H].
+struct XnOut {
+  float* tmp;
+  uint8_t* frag;
+  uint32_t nc, kpad;
+};
+
 template <int GR, bool PRE, bool HAS_D, class XL, class DL, class XO>
 __device__ void glue_tokens(int ntok, uint32_t H, float eps, const XL& xl, const DL& dl, const XO& xo,
-                            float* xn_out, float* red) {
+                            const XnOut& xn_out, float* red) {
   constexpr uint32_t NTHR = kConsumerWarps * 32;
   static_assert(kConsumerWarps <= 16, "consumers_sum buffers hold 16 partials");
   const float hf = static_cast<float>(H);
@@ -620,8 +666,26 @@ __device__ void glue_tokens(int ntok, uint32_t H, float eps, const XL& xl, const
 #pragma unroll
       for (int i = 0; i < GR; ++i) {
         const uint32_t h = threadIdx.x + i * NTHR;
-        if (h < H) xn_out[base + h] = bf16_round(xv[i] * inv);
+        if (h >= H) continue;
+        const float xn = bf16_round(xv[i] * inv);
+        if (xn_out.frag)
+          *reinterpret_cast<uint16_t*>(xn_out.frag + frag_offset(xn_out.nc, static_cast<uint32_t>(tok), h)) =
+              bf16_bits_rn(xn);
+        else
+          xn_out.tmp[base + h] = xn;
       }
+    }
+  }
+  if (PRE && xn_out.frag) {  // zero padding: k in [H, kpad) and columns [ntok, nc)
+    const uint32_t pad_k = xn_out.kpad - H;
+    for (uint32_t e = threadIdx.x; e < pad_k * xn_out.nc; e += NTHR) {
+      const uint32_t n = e % xn_out.nc, k = H + e / xn_out.nc;
+      *reinterpret_cast<uint16_t*>(xn_out.frag + frag_offset(xn_out.nc, n, k)) = 0;
+    }
+    const uint32_t extra = xn_out.nc - static_cast<uint32_t>(ntok);
+    for (uint32_t e = threadIdx.x; e < H * extra; e += NTHR) {
+      const uint32_t n = ntok + e % extra, k = e / extra;
+      *reinterpret_cast<uint16_t*>(xn_out.frag + frag_offset(xn_out.nc, n, k)) = 0;
     }
   }
   consumers_sync();
@@ -630,7 +694,7 @@ __device__ void glue_tokens(int ntok, uint32_t H, float eps, const XL& xl, const
 // GR chosen from H at run time (8 covers H <= 3840).
 template <bool PRE, bool HAS_D, class XL, class DL, class XO>
 __device__ __forceinline__ void glue(int ntok, uint32_t H, float eps, const XL& xl, const DL& dl, const XO& xo,
-                                     float* xn_out, float* red) {
+                                     const XnOut& xn_out, float* red) {
   if (H <= 8u * kConsumerWarps * 32)
     glue_tokens<8, PRE, HAS_D>(ntok, H, eps, xl, dl, xo, xn_out, red);
   else
@@ -710,12 +774,12 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_kernel(const FfnParams 
     trace_mark(p.trace, 6);
     const Bf16Out xo{blockIdx.x == 0 ? p.x_out : nullptr};
     const Bf16In xl{tma_in ? xraw : p.x_in};
+    const XnOut xn{nullptr, xs, static_cast<uint32_t>(NCA), p.gu.KT * 64};
     if (p.down_in)
-      glue<true, true>(p.ntok, p.H, p.eps, xl, F32In{tma_in ? draw : p.down_in}, xo, tmp, red);
+      glue<true, true>(p.ntok, p.H, p.eps, xl, F32In{tma_in ? draw : p.down_in}, xo, xn, red);
     else
-      glue<true, false>(p.ntok, p.H, p.eps, xl, NoIn{}, xo, tmp, red);
+      glue<true, false>(p.ntok, p.H, p.eps, xl, NoIn{}, xo, xn, red);
     trace_mark(p.trace, 7);
-    stage_frags<NCA, false>(xs, p.gu.KT, SmemSrc{tmp, p.ntok, p.H});
   } else {
     stage_frags<NCA, SPLIT>(xs, p.gu.KT, p.x);
   }
@@ -829,6 +893,7 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const Stac
   const Partition ptA = Partition::make(p.gu.RT, p.gu.KT, gridDim.x);
   const Partition ptB = Partition::make(p.dn.RT, p.dn.KT, gridDim.x);
   Shape::init_barriers(smem, p.nst);
+  const unsigned long long bar_base = threadIdx.x == 0 ? grid_base(p.bar, gridDim.x) : 0ull;
   if (lane == 0) {
     uint64_t a0, a1, b0, b1;
     ptA.warp_range(blockIdx.x, warp, a0, a1);
@@ -892,11 +957,12 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const Stac
       float* red = reinterpret_cast<float*>(xs + stack_xs_region(p.gu.KT, p.dn.KT, NC, p.H, p.ntok));
       uint16_t* xres = reinterpret_cast<uint16_t*>(red + 32);  // the residual stream (bf16)
       trace_mark(tr, 0);
+      const XnOut xn{nullptr, xs, static_cast<uint32_t>(NC), p.gu.KT * 64};
       if (l == 0)
-        glue<true, false>(p.ntok, p.H, p.eps, Bf16In{p.x_in}, NoIn{}, Bf16Out{xres}, tmp, red);
+        glue<true, false>(p.ntok, p.H, p.eps, Bf16In{p.x_in}, NoIn{}, Bf16Out{xres}, xn, red);
       else
-        glue<true, true>(p.ntok, p.H, p.eps, Bf16In{xres}, down_in(l - 1), Bf16Out{xres}, tmp, red);
-      stage_frags<NC, false>(xs, p.gu.KT, SmemSrc{tmp, p.ntok, p.H});
+        glue<true, true>(p.ntok, p.H, p.eps, Bf16In{xres}, down_in(l - 1), Bf16Out{xres}, xn, red);
+      (void)tmp;
     } else {
       const uint32_t xs_b = static_cast<uint32_t>(frag_bytes(p.dn.KT, NC));
       for (uint32_t o = threadIdx.x * 16; o < xs_b; o += NTHR * 16)
@@ -921,7 +987,7 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const Stac
       consumers_sync();
       trace_mark(tr, B ? 5 : 2);
     }
-    if (!grid_barrier(p.bar, gridDim.x, p.status) || !consumers_and(ok)) {
+    if (!grid_barrier_epoch(p.bar, gridDim.x, bar_base, i + 1, p.status) || !consumers_and(ok)) {
       ring.drain();
       return;
     }
@@ -931,7 +997,7 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const Stac
     float* red = reinterpret_cast<float*>(smem + base_smem_bytes(p.nst, p.ntok) +
                                           stack_xs_region(p.gu.KT, p.dn.KT, NC, p.H, p.ntok));
     glue<false, true>(p.ntok, p.H, p.eps, Bf16In{reinterpret_cast<uint16_t*>(red + 32)}, down_in(p.L - 1),
-                      Bf16Out{p.out}, nullptr, red);
+                      Bf16Out{p.out}, XnOut{}, red);
   }
 }
 
@@ -941,7 +1007,7 @@ __global__ void __launch_bounds__(kConsumerWarps * 32, 1)
     ffn_stack_finalize_kernel(int ntok, uint32_t H, const uint16_t* x_in, const float* down_in, uint16_t* x_out,
                               float eps) {
   __shared__ float red[32];
-  glue<false, true>(ntok, H, eps, Bf16In{x_in}, F32In{down_in}, Bf16Out{x_out}, nullptr, red);
+  glue<false, true>(ntok, H, eps, Bf16In{x_in}, F32In{down_in}, Bf16Out{x_out}, XnOut{}, red);
 }
 
 }  // namespace alv
