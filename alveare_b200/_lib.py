@@ -33,6 +33,8 @@ _u32 = _c.c_uint32
 _sz = _c.c_size_t
 
 # name -> (restype, argtypes); one entry per function declared in the header.
+IPC_BLOB_BYTES = 128  # ALV_IPC_BLOB_BYTES
+
 SIGNATURES = {
     "alv_version": (_i, []),
     "alv_ctx_create": (_i, [_i, _c.POINTER(_vp)]),
@@ -52,6 +54,8 @@ SIGNATURES = {
     "alv_ffn_stack_finalize": (_i, [_vp, _i, _i, _vp, _vp, _vp, _vp]),
     "alv_ffn_stack_create": (_i, [_vp, _c.POINTER(_u32), _i, _c.POINTER(_u32)]),
     "alv_ffn_stack_run": (_i, [_vp, _u32, _i, _vp, _vp, _vp]),
+    "alv_ffn_stack_exchange": (_i, [_vp, _u32, _i, _vp]),
+    "alv_ffn_stack_connect": (_i, [_vp, _u32, _i, _i, _vp]),
     "alv_run_gemv": (_i, [_vp, _u32, _i, _vp, _i, _vp, _i]),
     "alv_run_ffn": (_i, [_vp, _u32, _i, _vp, _i, _vp, _i]),
     "alv_gemv_noalloc": (_i, [_vp, _u32, _i, _vp, _i, _vp, _i, _vp]),

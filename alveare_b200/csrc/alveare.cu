@@ -45,6 +45,14 @@ struct Weight {
   LayerW* layers_dev = nullptr;
   uint8_t* ws = nullptr;
   size_t ws_bytes = 0;
+  // kind 3, tensor parallel: this rank's exchange region (cudaMalloc, shared
+  // with the peers by CUDA IPC) and every rank's region as mapped here
+  int world = 1, rank = 0;
+  bool connected = false, broken = false;
+  uint8_t* xlocal = nullptr;
+  uint32_t xslot = 0, xws_off = 0;
+  uint8_t* xr[kMaxRanks] = {};
+  unsigned char blob[ALV_IPC_BLOB_BYTES] = {};
 };
 
 }  // namespace
@@ -435,6 +443,10 @@ int check_status(alv_ctx* ctx, cudaStream_t st) {
     uint32_t t = 0;
     ALV_CUDA(ctx, cudaMemcpy(&t, w->ws, sizeof(t), cudaMemcpyDeviceToHost));
     if (t) ALV_CUDA(ctx, cudaMemset(w->ws, 0, stack_sync_bytes(w.get())));
+    // The peer-barrier counters of a tensor-parallel stack are out of step
+    // across ranks after a wait gave up: only re-creating it on every rank
+    // restores them.
+    if (t && w->world > 1) w->broken = true;
     s |= t;
   }
   if (s) {
@@ -642,6 +654,10 @@ int alv_weight_destroy(alv_ctx* ctx, alv_handle h) {
   cudaFree(w->b.dev);
   cudaFree(w->layers_dev);
   cudaFree(w->ws);
+  if (w->connected)
+    for (int q = 0; q < w->world; ++q)
+      if (q != w->rank && w->xr[q]) cudaIpcCloseMemHandle(w->xr[q]);
+  cudaFree(w->xlocal);
   ctx->weights[h - 1].reset();
   return ALV_OK;
 }
@@ -929,14 +945,14 @@ StackLayout stack_layout(alv_ctx* ctx, const Weight* w) {
   return o;
 }
 
-template <int NT, bool FAST>
+template <int NT, bool FAST, bool TP>
 int launch_stack_t(alv_ctx* ctx, StackParams p, cudaStream_t st) {
   const uint32_t nctas = static_cast<uint32_t>(ctx->num_sms);
   const size_t other = stack_smem_bytes(0, p.gu.KT, p.dn.KT, NT, p.H, p.ntok, p.dn.RT, nctas);
   p.nst = ring_stages(other);
   if (!p.nst) return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn_stack: H, I or ntok too large for shared memory");
   const size_t smem = stack_smem_bytes(p.nst, p.gu.KT, p.dn.KT, NT, p.H, p.ntok, p.dn.RT, nctas);
-  auto k = ffn_stack_kernel<NT, FAST>;
+  auto k = ffn_stack_kernel<NT, FAST, TP>;
   int rc = prepare_kernel(ctx, k, smem);
   if (rc) return rc;
   k<<<ctx->num_sms, kThreadsPerCta, smem, st>>>(p);
@@ -944,23 +960,37 @@ int launch_stack_t(alv_ctx* ctx, StackParams p, cudaStream_t st) {
   return ALV_OK;
 }
 
-template <bool FAST>
+template <bool FAST, bool TP>
 int launch_stack_f(alv_ctx* ctx, const StackParams& p, uint32_t nt, cudaStream_t st) {
   switch (nt) {
-    case 1: return launch_stack_t<1, FAST>(ctx, p, st);
-    case 2: return launch_stack_t<2, FAST>(ctx, p, st);
-    case 4: return launch_stack_t<4, FAST>(ctx, p, st);
+    case 1: return launch_stack_t<1, FAST, TP>(ctx, p, st);
+    case 2: return launch_stack_t<2, FAST, TP>(ctx, p, st);
+    case 4: return launch_stack_t<4, FAST, TP>(ctx, p, st);
   }
   return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn_stack: unsupported token count");
 }
+
+// Exchange slot of a tensor-parallel stack: [whole rows: kStackMaxTokens x H]
+// [CTA partials: #SMs x 2 x kStackMaxTokens x 16], in floats, 64-aligned.
+void exchange_shape(alv_ctx* ctx, const Weight* w, uint32_t* xslot, uint32_t* xws_off) {
+  const size_t rows = (static_cast<size_t>(kStackMaxTokens) * w->H + 63) / 64 * 64;
+  const size_t parts = static_cast<size_t>(ctx->num_sms) * 2 * kStackMaxTokens * 16;
+  *xws_off = static_cast<uint32_t>(rows);
+  *xslot = static_cast<uint32_t>((rows + parts + 63) / 64 * 64);
+}
+
+// Blob layout: [0, 64) cudaIpcMemHandle_t of the exchange region, [64, 80)
+// device UUID, [80, 100) u32 world, slot floats, I-slice width, layers, SMs
+// (the ranks must agree on all five: each launch passes layers x world x SMs
+// peer-barrier arrivals).
+constexpr size_t kBlobUuid = 64, kBlobWorld = 80;
+static_assert(sizeof(cudaIpcMemHandle_t) <= kBlobUuid, "IPC handle larger than its blob field");
 }  // namespace
 
 extern "C" int alv_ffn_stack_create(alv_ctx* ctx, const alv_handle* layers, int n, alv_handle* out) {
   if (!ctx || !layers || !out || n < 1) return fail(ctx, ALV_ERR_ARG, "ffn_stack_create: bad argument");
   const Weight* w0 = get_weight(ctx, layers[0], 2);
   if (!w0) return fail(ctx, ALV_ERR_HANDLE, "ffn_stack_create: layer 0 is not an ffn weight");
-  if (w0->i_begin != 0 || w0->i_end != w0->I)
-    return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn_stack_create: layers must hold the whole intermediate dimension");
   if (w0->H > 32u * kConsumerWarps * kGlueRegs)
     return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn_stack_create: H must be <= " + std::to_string(32u * kConsumerWarps * kGlueRegs));
   if (w0->a.m.RT + w0->b.m.RT > kMaxCounters) return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn_stack_create: too large");
@@ -1010,6 +1040,12 @@ extern "C" int alv_ffn_stack_run(alv_ctx* ctx, alv_handle h, int ntok, const uin
     return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn_stack_run: ntok must be 1.." + std::to_string(kStackMaxTokens));
   const Weight* w0 = get_weight(ctx, w->layers[0], 2);
   if (!w0) return fail(ctx, ALV_ERR_HANDLE, "ffn_stack_run: a layer was destroyed");
+  const bool tp = w->i_begin != 0 || w->i_end != w->I;
+  if (tp && !w->connected)
+    return fail(ctx, ALV_ERR_ARG, "ffn_stack_run: a stack of I-slices needs alv_ffn_stack_connect first");
+  if (w->broken)
+    return fail(ctx, ALV_ERR_ARG, "ffn_stack_run: a device wait of this tensor-parallel stack gave up earlier; "
+                                  "destroy and re-create it on every rank");
   for (alv_handle lh : w->layers)
     if (!get_weight(ctx, lh, 2) || get_weight(ctx, lh, 2)->act != w0->act)
       return fail(ctx, ALV_ERR_ARG, "ffn_stack_run: layers disagree on the activation");
@@ -1038,7 +1074,108 @@ extern "C" int alv_ffn_stack_run(alv_ctx* ctx, alv_handle h, int ntok, const uin
   p.trace = ctx->trace;
   const uint32_t nt = pow2_ceil(static_cast<uint32_t>(ntok));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  return p.gu.fast ? launch_stack_f<true>(ctx, p, nt, st) : launch_stack_f<false>(ctx, p, nt, st);
+  if (tp) {
+    p.world = static_cast<uint32_t>(w->world);
+    p.rank = static_cast<uint32_t>(w->rank);
+    for (int q = 0; q < w->world; ++q) p.xr[q] = w->xr[q];
+    p.xslot = w->xslot;
+    p.xws_off = w->xws_off;
+    return p.gu.fast ? launch_stack_f<true, true>(ctx, p, nt, st) : launch_stack_f<false, true>(ctx, p, nt, st);
+  }
+  return p.gu.fast ? launch_stack_f<true, false>(ctx, p, nt, st) : launch_stack_f<false, false>(ctx, p, nt, st);
+}
+
+extern "C" int alv_ffn_stack_exchange(alv_ctx* ctx, alv_handle h, int world, void* blob) {
+  if (!ctx || !blob) return fail(ctx, ALV_ERR_ARG, "ffn_stack_exchange: bad argument");
+  Weight* w = get_weight(ctx, h, 3);
+  if (!w) return fail(ctx, ALV_ERR_HANDLE, "ffn_stack_exchange: invalid handle (not an ffn stack)");
+  if (world < 2 || world > kMaxRanks)
+    return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn_stack_exchange: world must be 2.." + std::to_string(kMaxRanks));
+  if (w->xlocal) return fail(ctx, ALV_ERR_ARG, "ffn_stack_exchange: already called for this stack");
+  int rc = set_device(ctx);
+  if (rc) return rc;
+  exchange_shape(ctx, w, &w->xslot, &w->xws_off);
+  const size_t bytes = kXHeader + static_cast<size_t>(2) * world * w->xslot * 4;
+  ALV_CUDA(ctx, cudaMalloc(&w->xlocal, bytes));
+  ALV_CUDA(ctx, cudaMemset(w->xlocal, 0, bytes));
+  ALV_CUDA(ctx, cudaDeviceSynchronize());
+  cudaIpcMemHandle_t ih;
+  ALV_CUDA(ctx, cudaIpcGetMemHandle(&ih, w->xlocal));
+  cudaDeviceProp prop;
+  ALV_CUDA(ctx, cudaGetDeviceProperties(&prop, ctx->device));
+  std::memset(w->blob, 0, sizeof(w->blob));
+  std::memcpy(w->blob, &ih, sizeof(ih));
+  std::memcpy(w->blob + kBlobUuid, &prop.uuid, 16);
+  const uint32_t vals[5] = {static_cast<uint32_t>(world), w->xslot, w->i_end - w->i_begin,
+                            static_cast<uint32_t>(w->layers.size()), static_cast<uint32_t>(ctx->num_sms)};
+  std::memcpy(w->blob + kBlobWorld, vals, sizeof(vals));
+  w->world = world;
+  std::memcpy(blob, w->blob, ALV_IPC_BLOB_BYTES);
+  return ALV_OK;
+}
+
+extern "C" int alv_ffn_stack_connect(alv_ctx* ctx, alv_handle h, int rank, int world, const void* blobs) {
+  if (!ctx || !blobs) return fail(ctx, ALV_ERR_ARG, "ffn_stack_connect: bad argument");
+  Weight* w = get_weight(ctx, h, 3);
+  if (!w) return fail(ctx, ALV_ERR_HANDLE, "ffn_stack_connect: invalid handle (not an ffn stack)");
+  if (!w->xlocal || w->connected || world != w->world || rank < 0 || rank >= world)
+    return fail(ctx, ALV_ERR_ARG, "ffn_stack_connect: call once, after alv_ffn_stack_exchange with the same world");
+  const unsigned char* b = static_cast<const unsigned char*>(blobs);
+  auto blob_of = [&](int q) { return b + static_cast<size_t>(q) * ALV_IPC_BLOB_BYTES; };
+  if (std::memcmp(blob_of(rank), w->blob, ALV_IPC_BLOB_BYTES) != 0)
+    return fail(ctx, ALV_ERR_ARG, "ffn_stack_connect: blobs[rank] is not this stack's blob");
+  const uint32_t width = w->i_end - w->i_begin;
+  if (static_cast<uint64_t>(width) * world != w->I || w->i_begin != static_cast<uint32_t>(rank) * width)
+    return fail(ctx, ALV_ERR_SHAPE, "ffn_stack_connect: the layers are not I-slice `rank` of `world` equal slices");
+  for (int q = 0; q < world; ++q) {
+    uint32_t vals[5], mine[5];
+    std::memcpy(vals, blob_of(q) + kBlobWorld, sizeof(vals));
+    std::memcpy(mine, w->blob + kBlobWorld, sizeof(mine));
+    if (std::memcmp(vals, mine, sizeof(vals)) != 0)
+      return fail(ctx, ALV_ERR_SHAPE, "ffn_stack_connect: rank " + std::to_string(q) +
+                                          " differs in world, shape, layer count or SM count");
+    for (int o = 0; o < q; ++o)
+      if (std::memcmp(blob_of(q) + kBlobUuid, blob_of(o) + kBlobUuid, 16) == 0)
+        return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn_stack_connect: ranks " + std::to_string(o) + " and " +
+                                                  std::to_string(q) + " are on the same GPU");
+  }
+  int rc = set_device(ctx);
+  if (rc) return rc;
+  // Peers visible to this process must support native atomics over the link.
+  int ndev = 0;
+  ALV_CUDA(ctx, cudaGetDeviceCount(&ndev));
+  for (int d = 0; d < ndev; ++d) {
+    if (d == ctx->device) continue;
+    cudaDeviceProp prop;
+    ALV_CUDA(ctx, cudaGetDeviceProperties(&prop, d));
+    for (int q = 0; q < world; ++q) {
+      if (q == rank || std::memcmp(blob_of(q) + kBlobUuid, &prop.uuid, 16) != 0) continue;
+      int atomics = 0;
+      ALV_CUDA(ctx, cudaDeviceGetP2PAttribute(&atomics, cudaDevP2PAttrNativeAtomicSupported, ctx->device, d));
+      if (!atomics)
+        return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn_stack_connect: no native peer atomics to device " + std::to_string(d));
+    }
+  }
+  for (int q = 0; q < world; ++q) {
+    if (q == rank) {
+      w->xr[q] = w->xlocal;
+      continue;
+    }
+    cudaIpcMemHandle_t ih;
+    std::memcpy(&ih, blob_of(q), sizeof(ih));
+    void* ptr = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&ptr, ih, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (int o = 0; o < q; ++o)
+        if (o != rank && w->xr[o]) cudaIpcCloseMemHandle(w->xr[o]);
+      std::fill(w->xr, w->xr + kMaxRanks, nullptr);
+      return fail(ctx, ALV_ERR_CUDA, std::string("ffn_stack_connect: cudaIpcOpenMemHandle: ") + cudaGetErrorString(e));
+    }
+    w->xr[q] = static_cast<uint8_t*>(ptr);
+  }
+  w->rank = rank;
+  w->connected = true;
+  return ALV_OK;
 }
 
 // ===========================================================================

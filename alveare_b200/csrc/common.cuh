@@ -16,6 +16,7 @@ enum : uint32_t {
   kStatusMbarTimeout = 1u << 0,   // a bulk-copy completion wait gave up
   kStatusGridTimeout = 1u << 1,   // a grid-wide barrier wait gave up
   kStatusBadLaunch   = 1u << 2,   // kernel saw an inconsistent launch shape
+  kStatusPeerTimeout = 1u << 3,   // a barrier across tensor-parallel ranks gave up
 };
 
 // One second: every spin-wait in these kernels gives up after this long.

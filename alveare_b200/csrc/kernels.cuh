@@ -400,6 +400,48 @@ __device__ bool grid_barrier_epoch(GridBar* gb, uint32_t nblocks, unsigned long 
   return consumers_and(ok != 0);
 }
 
+// Barrier over every CTA of every rank of a tensor-parallel FFN stack
+// (ranks on distinct GPUs, one launch each).  Each CTA adds 1 to every
+// rank's counter (a system-scope release: this CTA's pushes to the peers
+// are visible before the count) and polls its own counter for
+// base + epoch * world * nblocks (system-scope acquire).  `base` is the own
+// counter at launch rounded down to a multiple of world * nblocks: before a
+// CTA's first arrival, only first-epoch arrivals of other CTAs can have
+// landed, and every launch adds a whole number of world * nblocks.
+__device__ __forceinline__ unsigned long long peer_base(const uint8_t* own, uint32_t world, uint32_t nblocks) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(own) : "memory");
+  const unsigned long long per = static_cast<unsigned long long>(world) * nblocks;
+  return v / per * per;
+}
+__device__ bool peer_barrier_epoch(uint8_t* const* xr, uint32_t world, uint32_t rank, uint32_t nblocks,
+                                   unsigned long long base, uint32_t epoch, uint32_t* status) {
+  consumers_sync();
+  int ok = 1;
+  if (threadIdx.x == 0) {
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    for (uint32_t q = 0; q < world; ++q)
+      asm volatile("red.relaxed.sys.global.add.u64 [%0], 1;" ::"l"(xr[q]) : "memory");
+    const unsigned long long target = base + static_cast<unsigned long long>(epoch) * world * nblocks;
+    const uint8_t* own = xr[rank];
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(own) : "memory");
+    if (v < target) {
+      const unsigned long long t0 = globaltimer_ns();
+      while (true) {
+        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(own) : "memory");
+        if (v >= target) break;
+        if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+          atomicOr(status, kStatusPeerTimeout);
+          ok = 0;
+          break;
+        }
+      }
+    }
+  }
+  return consumers_and(ok != 0);
+}
+
 // Sum over the consumer threads (all of them get the result) through `red`
 // (>= 16 floats).  One named barrier: consecutive calls must alternate
 // between two such buffers (a call's buffer is rewritten two calls later,
@@ -534,6 +576,7 @@ __device__ __forceinline__ void trace_mark(unsigned long long* trace, int i) {
 // every CTA computes identical values.  H <= 480 * GR.
 // ---------------------------------------------------------------------------
 constexpr int kGlueRegs = 16;
+constexpr int kMaxRanks = 8;  // tensor-parallel ranks of one FFN stack
 
 // Loaders: value of token tok at index h, flat index i = tok * H + h.
 struct Bf16In {   // bf16 values in memory written before the launch (or shared)
@@ -593,6 +636,37 @@ struct DownIn {
     return how == 0 ? a : (how == 1 ? (a + b) * sm : a * sm);
   }
 };
+// The down projection of a tensor-parallel layer: the sum over ranks, in
+// rank order, of each rank's DownIn (whole rows and CTA partials, all
+// pre-scaled) as the ranks pushed them into this GPU's exchange slots.
+// Every rank sums the same values in the same order, so every rank's
+// residual stream is identical.
+struct DownInX {
+  const float* slot0;       // this parity's slot of rank 0 (local memory)
+  uint32_t stride;          // floats from one rank's slot to the next
+  uint32_t world;
+  uint32_t ws_off;          // CTA partials within a slot
+  const uint2* split;
+  const uint32_t* cfirst;
+  const uint32_t* span;
+  uint32_t slot_floats;
+  __device__ __forceinline__ void load(uint32_t tok, uint32_t h, size_t i, float& a, float& b, uint32_t& how) const {
+    float v = 0.f;
+    for (uint32_t q = 0; q < world; ++q) {
+      const float* d = slot0 + static_cast<size_t>(q) * stride;
+      const DownIn di{d, d + ws_off, split, cfirst, span, slot_floats, 1.0f};
+      float x, y;
+      uint32_t hw;
+      di.load(tok, h, i, x, y, hw);
+      const float t = di.combine(x, y, hw);
+      v = q ? v + t : t;
+    }
+    a = v;
+    b = 0.f;
+    how = 0;
+  }
+  __device__ __forceinline__ float combine(float a, float, uint32_t) const { return a; }
+};
 struct NoIn {
   __device__ __forceinline__ void load(uint32_t, uint32_t, size_t, float& a, float& b, uint32_t& how) const {
     a = b = 0.f;
@@ -619,7 +693,7 @@ struct XnOut {
 
 template <int GR, bool PRE, bool HAS_D, class XL, class DL, class XO>
 __device__ void glue_tokens(int ntok, uint32_t H, float eps, const XL& xl, const DL& dl, const XO& xo,
-                            const XnOut& xn_out, float* red) {
+                            const XnOut& xn_out, float* red, unsigned long long* tr) {
   constexpr uint32_t NTHR = kConsumerWarps * 32;
   static_assert(kConsumerWarps <= 16, "consumers_sum buffers hold 16 partials");
   const float hf = static_cast<float>(H);
@@ -643,11 +717,13 @@ __device__ void glue_tokens(int ntok, uint32_t H, float eps, const XL& xl, const
     }
 #pragma unroll
     for (int i = 0; i < GR; ++i) dv[i] = HAS_D ? bf16_round(dl.combine(dv[i], db[i], (how >> (2 * i)) & 3)) : 0.f;
+    if (tok == 0) trace_mark(tr, 9);
     if (HAS_D) {
       float ss = 0.f;
 #pragma unroll
       for (int i = 0; i < GR; ++i) ss = fmaf(dv[i], dv[i], ss);
       ss = consumers_sum(ss, red + 16 * (rs++ & 1));
+      if (tok == 0) trace_mark(tr, 10);
       const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, hf), eps)));
 #pragma unroll
       for (int i = 0; i < GR; ++i) xv[i] = bf16_round(xv[i] + bf16_round(dv[i] * inv));
@@ -662,6 +738,7 @@ __device__ void glue_tokens(int ntok, uint32_t H, float eps, const XL& xl, const
 #pragma unroll
       for (int i = 0; i < GR; ++i) ss = fmaf(xv[i], xv[i], ss);
       ss = consumers_sum(ss, red + 16 * (rs++ & 1));
+      if (tok == 0) trace_mark(tr, 11);
       const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, hf), eps)));
 #pragma unroll
       for (int i = 0; i < GR; ++i) {
@@ -688,17 +765,20 @@ __device__ void glue_tokens(int ntok, uint32_t H, float eps, const XL& xl, const
       *reinterpret_cast<uint16_t*>(xn_out.frag + frag_offset(xn_out.nc, n, k)) = 0;
     }
   }
+  trace_mark(tr, 12);
   consumers_sync();
 }
 
 // GR chosen from H at run time (8 covers H <= 3840).
+// tr: optional phase stamps [9] down loaded, [10] its norm reduced, [11] x's
+// norm reduced, [12] xn written (first token).
 template <bool PRE, bool HAS_D, class XL, class DL, class XO>
 __device__ __forceinline__ void glue(int ntok, uint32_t H, float eps, const XL& xl, const DL& dl, const XO& xo,
-                                     const XnOut& xn_out, float* red) {
+                                     const XnOut& xn_out, float* red, unsigned long long* tr = nullptr) {
   if (H <= 8u * kConsumerWarps * 32)
-    glue_tokens<8, PRE, HAS_D>(ntok, H, eps, xl, dl, xo, xn_out, red);
+    glue_tokens<8, PRE, HAS_D>(ntok, H, eps, xl, dl, xo, xn_out, red, tr);
   else
-    glue_tokens<kGlueRegs, PRE, HAS_D>(ntok, H, eps, xl, dl, xo, xn_out, red);
+    glue_tokens<kGlueRegs, PRE, HAS_D>(ntok, H, eps, xl, dl, xo, xn_out, red, tr);
 }
 
 template <int NT, bool SPLIT, bool FAST>
@@ -843,7 +923,19 @@ struct StackParams {
   uint32_t* status;
   uint32_t nst;
   unsigned long long* trace;  // optional: phase stamps of layer 1
+  // Tensor parallelism (ffn_stack_kernel<..., TP = true>): rank `rank` of
+  // `world` holds an I-slice of every layer.  xr[q] is rank q's exchange
+  // region as mapped on this GPU (xr[rank] is this GPU's own):
+  //   [peer-barrier counter u64 @0][slots @kXHeader: parity x world x xslot floats]
+  // Slot (parity, q) of every region holds rank q's down output of the
+  // layers of that parity: [whole rows: ntok x H][CTA partials @xws_off].
+  uint32_t world, rank;
+  uint8_t* xr[kMaxRanks];
+  uint32_t xslot, xws_off;
 };
+
+// Exchange region header: the peer-barrier counter, padded.
+constexpr size_t kXHeader = 256;
 
 // Epilogue of either stack phase: gate/up -> activation into act (phase A),
 // or down rows into the fp32 down vector (phase B).
@@ -854,6 +946,8 @@ struct StackEpi {
   uint32_t I, H, ncb;
   float sm;
   int fn;
+  float pmul;  // parked CTA partials are stored times pmul (1, or sm when the sum is taken across ranks)
+  __device__ __forceinline__ float park(float v) const { return v * pmul; }
   __device__ __forceinline__ void apply(uint32_t r, int g, int tok, float vg, float vg8) const {
     if (down_phase) {
       RowsEpi{down, nullptr, H, H, sm}.apply(r, g, tok, vg, vg8);
@@ -882,18 +976,56 @@ __host__ __device__ inline size_t stack_smem_bytes(uint32_t nst, uint32_t KTA, u
   return stack_tables_offset(nst, KTA, KTB, nc, H, ntok) + (static_cast<size_t>(RTB) * 3 + nctas) * 4;
 }
 
-template <int NT, bool FAST>
-__global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const StackParams p) {
+// Slot (parity, owner) of rank `region`'s exchange region (TP stacks).
+__device__ __forceinline__ float* xslot_ptr(const StackParams& p, uint32_t region, uint32_t par, uint32_t owner) {
+  return reinterpret_cast<float*>(p.xr[region] + kXHeader) + (static_cast<size_t>(par) * p.world + owner) * p.xslot;
+}
+
+// Tensor parallelism: copy what this CTA wrote into its own rank's slot --
+// its whole down rows [row0, row1) and its two CTA-partial slots -- to the
+// same offsets of every peer's slot (plain stores over NVLink, consecutive
+// threads on consecutive floats).
+__device__ void push_down(const StackParams& p, uint32_t par, uint32_t row0, uint32_t row1) {
+  constexpr uint32_t NTHR = kConsumerWarps * 32;
+  consumers_sync();  // every warp's rows and partials are written
+  const float* src = xslot_ptr(p, p.rank, par, p.rank);
+  const uint32_t H = p.H, ntok = static_cast<uint32_t>(p.ntok);
+  const uint32_t h0 = min(row0 * 16, H), h1 = min(row1 * 16, H), nr = h1 - h0;
+  const uint32_t sf = ntok * 16, n_rows = nr * ntok, n = n_rows + 2 * sf;
+  for (uint32_t e = threadIdx.x; e < n; e += NTHR) {
+    size_t off;
+    if (e < n_rows) {
+      const uint32_t tok = e / nr;
+      off = static_cast<size_t>(tok) * H + h0 + (e - tok * nr);
+    } else {
+      off = p.xws_off + static_cast<size_t>(blockIdx.x) * 2 * sf + (e - n_rows);
+    }
+    const float v = __ldcg(src + off);
+    for (uint32_t q = 0; q < p.world; ++q)
+      if (q != p.rank) xslot_ptr(p, q, par, p.rank)[off] = v;
+  }
+}
+
+// TP = true: one rank of a tensor-parallel stack (see StackParams).  Phase B
+// writes this rank's partial down projection into its own exchange slot,
+// pushes it to every peer and meets all ranks' CTAs at a peer barrier; the
+// next glue sums the ranks' slots in rank order.  The slots alternate
+// between two parities by the global count of peer barriers, so a rank that
+// runs ahead writes the other parity from the one its peers still read.
+template <int NT, bool FAST, bool TP>
+__global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const __grid_constant__ StackParams p) {
   constexpr int NC = NT;  // bf16 activations: one fragment column per token
   constexpr uint32_t NTHR = kConsumerWarps * 32;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint32_t wk[kConsumerWarps][4];  // per warp: a0 a1 b0 b1
   __shared__ StackWork sw[kConsumerWarps];
+  __shared__ unsigned long long xbase_s;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const Partition ptA = Partition::make(p.gu.RT, p.gu.KT, gridDim.x);
   const Partition ptB = Partition::make(p.dn.RT, p.dn.KT, gridDim.x);
   Shape::init_barriers(smem, p.nst);
   const unsigned long long bar_base = threadIdx.x == 0 ? grid_base(p.bar, gridDim.x) : 0ull;
+  if (TP && threadIdx.x == 0) xbase_s = peer_base(p.xr[p.rank], p.world, gridDim.x);
   if (lane == 0) {
     uint64_t a0, a1, b0, b1;
     ptA.warp_range(blockIdx.x, warp, a0, a1);
@@ -930,6 +1062,18 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const Stac
     split[r] = o;
   }
   __syncthreads();
+  // TP: this CTA's whole down rows [prow0, prow1) (pushed to the peers), and
+  // the parity of layer 0's exchange slots.
+  uint32_t prow0 = 0, prow1 = 0, xpar0 = 0;
+  unsigned long long xbase = 0;
+  if (TP) {
+    const uint64_t c0 = ptB.cta_begin(blockIdx.x), c1 = ptB.cta_begin(blockIdx.x + 1);
+    prow0 = static_cast<uint32_t>((c0 + p.dn.KT - 1) / p.dn.KT);
+    prow1 = static_cast<uint32_t>(c1 / p.dn.KT);
+    if (prow1 < prow0) prow1 = prow0;
+    xbase = xbase_s;
+    xpar0 = static_cast<uint32_t>(xbase / (static_cast<unsigned long long>(p.world) * gridDim.x)) & 1u;
+  }
   const uint32_t* my = wk[warp];
   ConsumerRing<kUnitsPerStage, StackWork> ring;
   ring.setup(smem, p.nst, warp, p.L * ((my[1] - my[0]) + (my[3] - my[2])), &sw[warp]);
@@ -937,6 +1081,10 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const Stac
   auto down_in = [&](uint32_t l) {
     return DownIn{p.down, p.fxB.ws, split, cfirst, span, static_cast<uint32_t>(p.ntok) * 16,
                   __ldg(&p.layers[l].dn_mul)};
+  };
+  auto down_in_x = [&](uint32_t l) {
+    return DownInX{xslot_ptr(p, p.rank, (xpar0 + l) & 1u, 0), p.xslot, p.world, p.xws_off, split, cfirst, span,
+                   static_cast<uint32_t>(p.ntok) * 16};
   };
   // The act padding (k in [I, 64*dn.KT)) must read as zero in phase B.
   if (blockIdx.x == 0) {
@@ -952,17 +1100,19 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const Stac
     const bool B = i & 1;
     uint8_t* xs = smem + base_smem_bytes(p.nst, p.ntok);
     unsigned long long* tr = (l == 1) ? p.trace : nullptr;
+    float* bdown = TP ? xslot_ptr(p, p.rank, (xpar0 + l) & 1u, p.rank) : p.down;
     if (!B) {
-      float* tmp = reinterpret_cast<float*>(xs + frag_bytes(p.gu.KT, NC));
       float* red = reinterpret_cast<float*>(xs + stack_xs_region(p.gu.KT, p.dn.KT, NC, p.H, p.ntok));
       uint16_t* xres = reinterpret_cast<uint16_t*>(red + 32);  // the residual stream (bf16)
       trace_mark(tr, 0);
       const XnOut xn{nullptr, xs, static_cast<uint32_t>(NC), p.gu.KT * 64};
-      if (l == 0)
+      if (l == 0) {
         glue<true, false>(p.ntok, p.H, p.eps, Bf16In{p.x_in}, NoIn{}, Bf16Out{xres}, xn, red);
-      else
-        glue<true, true>(p.ntok, p.H, p.eps, Bf16In{xres}, down_in(l - 1), Bf16Out{xres}, xn, red);
-      (void)tmp;
+      } else if constexpr (TP) {
+        glue<true, true>(p.ntok, p.H, p.eps, Bf16In{xres}, down_in_x(l - 1), Bf16Out{xres}, xn, red, tr);
+      } else {
+        glue<true, true>(p.ntok, p.H, p.eps, Bf16In{xres}, down_in(l - 1), Bf16Out{xres}, xn, red, tr);
+      }
     } else {
       const uint32_t xs_b = static_cast<uint32_t>(frag_bytes(p.dn.KT, NC));
       for (uint32_t o = threadIdx.x * 16; o < xs_b; o += NTHR * 16)
@@ -970,8 +1120,10 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const Stac
     }
     consumers_sync();
     trace_mark(tr, B ? 4 : 1);
-    const StackEpi epi{B, p.act, p.down, p.I, p.H, NC, B ? __ldg(&p.layers[l].dn_mul) : __ldg(&p.layers[l].gu_mul), p.fn};
+    const float sm = B ? __ldg(&p.layers[l].dn_mul) : __ldg(&p.layers[l].gu_mul);
+    const StackEpi epi{B, p.act, bdown, p.I, p.H, NC, sm, p.fn, TP ? sm : 1.0f};
     Fixup fx = B ? p.fxB : p.fxA;
+    if (TP && B) fx.ws = bdown + p.xws_off;
     fx.part = reinterpret_cast<float*>(smem + ring_smem_bytes(p.nst));
     const bool ok = consume_range<NC, false, FAST>(ring, B ? p.dn : p.gu, my[B ? 2 : 0], my[B ? 3 : 1], xs, fx,
                                                    p.ntok, epi, p.status);
@@ -983,11 +1135,17 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const Stac
       cta_fixup<true>(ptB, &wk[0][2], fx, p.ntok, epi);  // rows shared between CTAs: summed by the next glue
     else
       cta_fixup(ptA, &wk[0][0], fx, p.ntok, epi);
+    if (TP && B) push_down(p, (xpar0 + l) & 1u, prow0, prow1);
     if (tr) {
       consumers_sync();
       trace_mark(tr, B ? 5 : 2);
     }
-    if (!grid_barrier_epoch(p.bar, gridDim.x, bar_base, i + 1, p.status) || !consumers_and(ok)) {
+    bool bar_ok;
+    if (TP && B)
+      bar_ok = peer_barrier_epoch(p.xr, p.world, p.rank, gridDim.x, xbase, l + 1, p.status);
+    else
+      bar_ok = grid_barrier_epoch(p.bar, gridDim.x, bar_base, TP ? l + 1 : i + 1, p.status);
+    if (!bar_ok || !consumers_and(ok)) {
       ring.drain();
       return;
     }
@@ -996,8 +1154,11 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const Stac
   if (blockIdx.x == 0) {
     float* red = reinterpret_cast<float*>(smem + base_smem_bytes(p.nst, p.ntok) +
                                           stack_xs_region(p.gu.KT, p.dn.KT, NC, p.H, p.ntok));
-    glue<false, true>(p.ntok, p.H, p.eps, Bf16In{reinterpret_cast<uint16_t*>(red + 32)}, down_in(p.L - 1),
-                      Bf16Out{p.out}, XnOut{}, red);
+    const Bf16In xl{reinterpret_cast<uint16_t*>(red + 32)};
+    if constexpr (TP)
+      glue<false, true>(p.ntok, p.H, p.eps, xl, down_in_x(p.L - 1), Bf16Out{p.out}, XnOut{}, red);
+    else
+      glue<false, true>(p.ntok, p.H, p.eps, xl, down_in(p.L - 1), Bf16Out{p.out}, XnOut{}, red);
   }
 }
 

@@ -654,6 +654,9 @@ __device__ void cta_fixup(const Partition& pt, const uint32_t* wr, const Fixup& 
       }
       if (inside) {
         epi.apply(r, g, tok, vg, vg8);
+      } else if constexpr (DEFER) {  // the epilogue may pre-scale parked partials
+        cpart[tok * 16 + g] = epi.park(vg);
+        cpart[tok * 16 + g + 8] = epi.park(vg8);
       } else {
         cpart[tok * 16 + g] = vg;
         cpart[tok * 16 + g + 8] = vg8;

@@ -7,12 +7,15 @@ GPU: per layer ``x2 = rmsnorm(x)``, ``down = FFN(x2)``,
 ``x = x + rmsnorm(down)`` (unit norm weights), with every step on the device.
 Tensor parallelism splits each FFN's intermediate dimension over the ranks
 (the reference's I-split across AIE cores, kernels/ffn_fused/ffn_fused.py:46-60,
-lifted to GPUs); the per-layer partial down projections are summed with one
-NCCL all-reduce of H fp32 values (the reference's host partial sum,
-runtime/cpp/src/npu.cpp:360-377).  On one GPU the whole step is a single
-persistent kernel (alv_ffn_stack_run) that streams every layer's weights back
-to back; with tensor parallelism each layer is one kernel followed by the
-all-reduce.  A step is captured once into a CUDA graph and replayed.
+lifted to GPUs), and the per-layer partial down projections are summed across
+ranks (the reference's host partial sum, runtime/cpp/src/npu.cpp:360-377).
+The whole step is a single persistent kernel per GPU (alv_ffn_stack_run) that
+streams every layer's weights back to back; with tensor parallelism that
+kernel pushes each layer's partial down projection to every peer GPU over
+NVLink and meets the peers at a barrier, so no collective runs between
+layers.  The per-layer path (fused=False: one kernel per layer, and with
+tensor parallelism one NCCL all-reduce of H fp32 values per layer) is kept as
+the baseline.  A step is captured once into a CUDA graph and replayed.
 """
 from __future__ import annotations
 
@@ -50,9 +53,7 @@ class FFNStack:
                  activation: str = "gelu", fused: bool = True):
         self.H, self.I, self.device, self.rank, self.world = H, I, device, rank, world
         self.activation = activation
-        # one launch per step (single GPU only: the per-layer all-reduce of
-        # tensor parallelism runs between layer kernels)
-        self.fused = fused and world == 1
+        self.fused = fused
         self.stack_handle = 0
         self.i_begin, self.i_end = tp_slice(I, rank, world)
         self.layers: list[FusedFFNWeight] = []
@@ -82,7 +83,25 @@ class FFNStack:
             h = ctypes.c_uint32()
             ctx.check(ctx.lib.alv_ffn_stack_create(ctx.ptr, arr, n, ctypes.byref(h)), "alv_ffn_stack_create")
             self.stack_handle = h.value
+            if self.world > 1:
+                self._connect()
         return self.stack_handle
+
+    def _connect(self) -> None:
+        """Map every rank's exchange region (collective over the process
+        group): export this rank's blob, all-gather, connect, then a barrier
+        so that no rank's first launch waits on a peer still connecting."""
+        import torch.distributed as dist
+        ctx = self.ctx
+        blob = (ctypes.c_ubyte * _lib.IPC_BLOB_BYTES)()
+        ctx.check(ctx.lib.alv_ffn_stack_exchange(ctx.ptr, self.stack_handle, self.world, blob),
+                  "alv_ffn_stack_exchange")
+        blobs: list = [None] * self.world
+        dist.all_gather_object(blobs, bytes(blob))
+        allb = (ctypes.c_ubyte * (_lib.IPC_BLOB_BYTES * self.world)).from_buffer_copy(b"".join(blobs))
+        ctx.check(ctx.lib.alv_ffn_stack_connect(ctx.ptr, self.stack_handle, self.rank, self.world, allb),
+                  "alv_ffn_stack_connect")
+        dist.barrier()
 
     def weight_bytes(self) -> int:
         """Algorithmic weight bytes of the whole stack (all ranks): 18 B per 32 weights."""
@@ -147,9 +166,15 @@ class FFNStack:
         self.graph = None
 
     def free(self) -> None:
-        """Release the stack handle and the layers' device memory."""
+        """Release the stack handle and the layers' device memory.  With
+        tensor parallelism this is collective: a barrier first, so no peer
+        still runs a step that writes into this rank's exchange region."""
         self.graph = None
         ctx = self.ctx
+        if self.stack_handle and self.world > 1 and self.fused:
+            import torch.distributed as dist
+            torch.cuda.synchronize(self.device)
+            dist.barrier()
         if self.stack_handle:
             ctx.check(ctx.lib.alv_weight_destroy(ctx.ptr, self.stack_handle), "alv_weight_destroy")
             self.stack_handle = 0

@@ -6,8 +6,9 @@ intermediate 15360, GeGLU, Q4 group-32 weights quantized from N(0, 0.02)
 (synthetic, seeded; generated and quantized on the GPU).  One step = one
 decode token through all 48 FFN half-blocks (rmsnorm -> fused FFN ->
 rmsnorm -> residual).  With --gpus N (torchrun) each rank holds 1/N of the
-intermediate dimension and the per-layer partial down projections are
-all-reduced over NCCL.
+intermediate dimension; the step is still one kernel launch per GPU, which
+pushes each layer's partial down projection to the peer GPUs over NVLink and
+sums the ranks' partials in rank order (no collective between layers).
 
 Metric: achieved HBM GB/s of algorithmic bytes -- 18 B per
 32 weights, activations counted once -- for the whole job; tokens/s is

@@ -156,8 +156,9 @@ int alv_ffn_stack_finalize(alv_ctx* ctx, int ntok, int H, const uint16_t* x_in,
  * decode step (runtime/cpp/src/model.cpp:404 inside the layer loop,
  * runtime/py/model.py:782-806) over n FFN weights, i.e. alv_ffn_layer for
  * layer 0..n-1 followed by alv_ffn_stack_finalize, with identical results.
- * The layers must share H, I, activation and dequant path and hold the whole
- * intermediate dimension (i_begin = 0, i_end = I); the stack references them
+ * The layers must share H, I, I-slice, activation and dequant path; a stack
+ * of I-slices (i_begin, i_end not 0, I) runs only once connected to its
+ * tensor-parallel peers (alv_ffn_stack_connect).  The stack references them
  * (destroy the stack with alv_weight_destroy before its layers).  It owns its
  * workspace, so a captured launch stays valid.  No counterpart handle exists
  * in the reference (its registry runs one FFN call per layer). */
@@ -167,6 +168,29 @@ int alv_ffn_stack_create(alv_ctx* ctx, const alv_handle* layers, int n, alv_hand
  * (ALV_ERR_UNSUPPORTED when the activations do not fit in shared memory). */
 int alv_ffn_stack_run(alv_ctx* ctx, alv_handle stack, int ntok, const uint16_t* x_in, uint16_t* out,
                       void* stream);
+
+/* Tensor-parallel FFN stack over the GPUs of one node, one process per GPU.
+ * The reference splits each FFN's intermediate dimension over compute tiles
+ * and sums the partial down projections on the host
+ * (kernels/ffn_fused/ffn_fused.py:46-60, runtime/cpp/src/npu.cpp:360-377).
+ * Here rank q's stack holds the layers of I-slice q (alv_ffn_create with
+ * i_begin / i_end, equal slices), and inside the one stack launch each
+ * layer's partial down projection is pushed to every peer GPU over NVLink
+ * and summed there in rank order, so no collective library runs between
+ * layers and every rank produces the identical `out`.  Setup, on every
+ * rank:
+ *   alv_ffn_stack_exchange(ctx, stack, world, blob)   (ALV_IPC_BLOB_BYTES)
+ *   all-gather the blobs in rank order (any host transport)
+ *   alv_ffn_stack_connect(ctx, stack, rank, world, blobs)
+ *   a host barrier; then alv_ffn_stack_run on every rank with the same x_in.
+ * The ranks' launches wait for one another, so each rank must be on its own
+ * GPU (connect checks the device UUIDs).  A rank launched more than a second
+ * after the others makes every rank's launch give up (ALV_ERR_TIMEOUT at
+ * alv_sync_status); the stack is then unusable (ALV_ERR_ARG) and has to be
+ * destroyed and re-created on every rank.  No counterpart in the reference. */
+#define ALV_IPC_BLOB_BYTES 128
+int alv_ffn_stack_exchange(alv_ctx* ctx, alv_handle stack, int world, void* blob);
+int alv_ffn_stack_connect(alv_ctx* ctx, alv_handle stack, int rank, int world, const void* blobs);
 
 /* Allocation-free gemv: same arithmetic and arguments as alv_gemv, for
  * callers that must not allocate device memory while they run (a decode
@@ -192,8 +216,10 @@ int alv_gemv_noalloc(alv_ctx* ctx, alv_handle h, int ntok, const void* x, int x_
  * phase done; with the layer glue also [6] inputs landed, [7] glue done.
  * alv_ffn_stack_run writes the same stamps for its second layer ([0] glue
  * start, [1]-[5] as above, [6] the layer's last barrier passed, [7] / [8]
- * gate/up / down units streamed, before the split-K reduction).  Slots
- * [9]-[15] are unused.  NULL turns tracing off (the default). */
+ * gate/up / down units streamed, before the split-K reduction; inside its
+ * glue [9] down loaded, [10] / [11] the norms of down / x reduced, [12] the
+ * normalized x written).  Slots [13]-[15] are unused.  NULL turns tracing
+ * off (the default). */
 int alv_set_trace(alv_ctx* ctx, uint64_t* trace);
 
 /* ---- host-buffer convenience (synchronous, like NpuRegistry::run_gemv) ---- */

@@ -179,3 +179,33 @@ def test_ffnstack_fused_and_per_layer_agree():
         assert st.launches == (1 if fused else L + 1)
         st.free()
     assert np.array_equal(outs[0], outs[1])
+
+
+def test_tp_stack_connect_rejects_ranks_on_one_gpu():
+    """Two I-slice stacks in one process on one GPU: connect refuses (ranks of
+    the tensor-parallel stack kernel wait for one another), and a slice stack
+    that is not connected refuses to run.  No kernel is launched."""
+    H, I = 256, 1024
+    (layer,) = make_layers(H, I, 1, 60)
+    ws = [FusedFFNWeight(*layer, H, I, "gelu", i_begin=b, i_end=b + I // 2) for b in (0, I // 2)]
+    ctx = ws[0].ctx
+    hs, blobs = [], b""
+    for w in ws:
+        arr = (ctypes.c_uint32 * 1)(w.handle)
+        h = ctypes.c_uint32()
+        ctx.check(ctx.lib.alv_ffn_stack_create(ctx.ptr, arr, 1, ctypes.byref(h)), "alv_ffn_stack_create")
+        hs.append(h.value)
+    x = torch.zeros(H, dtype=torch.int16, device="cuda")
+    assert ctx.lib.alv_ffn_stack_run(ctx.ptr, hs[0], 1, x.data_ptr(), x.data_ptr(), None) == 1  # not connected
+    for h in hs:
+        blob = (ctypes.c_ubyte * _lib.IPC_BLOB_BYTES)()
+        ctx.check(ctx.lib.alv_ffn_stack_exchange(ctx.ptr, h, 2, blob), "alv_ffn_stack_exchange")
+        blobs += bytes(blob)
+    allb = (ctypes.c_ubyte * len(blobs)).from_buffer_copy(blobs)
+    assert ctx.lib.alv_ffn_stack_connect(ctx.ptr, hs[0], 0, 2, allb) == 6  # ALV_ERR_UNSUPPORTED
+    assert b"same GPU" in ctx.lib.alv_last_error(ctx.ptr)
+    assert ctx.lib.alv_ffn_stack_connect(ctx.ptr, hs[1], 0, 2, allb) == 1  # blobs[0] is not its blob
+    for h in hs:
+        ctx.check(ctx.lib.alv_weight_destroy(ctx.ptr, h), "destroy stack")
+    for w in ws:
+        w.free()
