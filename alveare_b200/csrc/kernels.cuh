@@ -400,29 +400,31 @@ __device__ bool grid_barrier_epoch(GridBar* gb, uint32_t nblocks, unsigned long 
   return consumers_and(ok != 0);
 }
 
-// Barrier over every CTA of every rank of a tensor-parallel FFN stack
-// (ranks on distinct GPUs, one launch each).  Each CTA adds 1 to every
-// rank's counter (a system-scope release: this CTA's pushes to the peers
-// are visible before the count) and polls its own counter for
-// base + epoch * world * nblocks (system-scope acquire).  `base` is the own
-// counter at launch rounded down to a multiple of world * nblocks: before a
-// CTA's first arrival, only first-epoch arrivals of other CTAs can have
-// landed, and every launch adds a whole number of world * nblocks.
-__device__ __forceinline__ unsigned long long peer_base(const uint8_t* own, uint32_t world, uint32_t nblocks) {
+// Exchange step of a tensor-parallel FFN stack (ranks on distinct GPUs, one
+// launch each), after the rank's own grid barrier: CTA 0 -- which the grid
+// barrier ordered after every local CTA's pushes -- issues one system-scope
+// release (fence.acq_rel.sys) and adds 1 to every rank's counter, its own
+// included; every CTA then polls its own counter (system-scope acquire) for
+// base + epoch * world.  One system fence per rank and exchange, not one per
+// CTA.  `base` is the own counter at launch rounded down to a multiple of
+// world: before this launch's CTA 0 signals (which needs every local CTA past
+// the first grid barrier, so after each CTA read its base) at most the
+// other ranks' world - 1 first-exchange signals can have landed.
+__device__ __forceinline__ unsigned long long peer_base(const uint8_t* own, uint32_t world) {
   unsigned long long v;
   asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(own) : "memory");
-  const unsigned long long per = static_cast<unsigned long long>(world) * nblocks;
-  return v / per * per;
+  return v / world * world;
 }
-__device__ bool peer_barrier_epoch(uint8_t* const* xr, uint32_t world, uint32_t rank, uint32_t nblocks,
-                                   unsigned long long base, uint32_t epoch, uint32_t* status) {
-  consumers_sync();
+__device__ bool peer_exchange(uint8_t* const* xr, uint32_t world, uint32_t rank, unsigned long long base,
+                              uint32_t epoch, uint32_t* status) {
   int ok = 1;
   if (threadIdx.x == 0) {
-    asm volatile("fence.acq_rel.sys;" ::: "memory");
-    for (uint32_t q = 0; q < world; ++q)
-      asm volatile("red.relaxed.sys.global.add.u64 [%0], 1;" ::"l"(xr[q]) : "memory");
-    const unsigned long long target = base + static_cast<unsigned long long>(epoch) * world * nblocks;
+    if (blockIdx.x == 0) {
+      asm volatile("fence.acq_rel.sys;" ::: "memory");
+      for (uint32_t q = 0; q < world; ++q)
+        asm volatile("red.relaxed.sys.global.add.u64 [%0], 1;" ::"l"(xr[q]) : "memory");
+    }
+    const unsigned long long target = base + static_cast<unsigned long long>(epoch) * world;
     const uint8_t* own = xr[rank];
     unsigned long long v;
     asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(own) : "memory");
@@ -691,6 +693,16 @@ struct XnOut {
   uint32_t nc, kpad;
 };
 
+// Copy `bytes` (a multiple of 16) from global memory (through L2) into
+// shared memory with the consumer threads, 16 bytes per thread and step.
+// (Holding several loads in registers before the stores makes the stack
+// kernel spill.)
+__device__ __forceinline__ void stage_from_l2(uint8_t* dst, const uint8_t* src, uint32_t bytes) {
+  constexpr uint32_t NTHR = kConsumerWarps * 32, STEP = NTHR * 16;
+  for (uint32_t o = threadIdx.x * 16; o < bytes; o += STEP)
+    *reinterpret_cast<uint4*>(dst + o) = __ldcg(reinterpret_cast<const uint4*>(src + o));
+}
+
 template <int GR, bool PRE, bool HAS_D, class XL, class DL, class XO>
 __device__ void glue_tokens(int ntok, uint32_t H, float eps, const XL& xl, const DL& dl, const XO& xo,
                             const XnOut& xn_out, float* red, unsigned long long* tr) {
@@ -880,8 +892,7 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_kernel(const FfnParams 
     return;
   }
   // act is already in fragment order: stage it with 16-byte copies through L2.
-  for (uint32_t o = threadIdx.x * 16; o < xs_bytes_b; o += NTHR * 16)
-    *reinterpret_cast<uint4*>(xs + o) = __ldcg(reinterpret_cast<const uint4*>(p.act + o));
+  stage_from_l2(xs, p.act, static_cast<uint32_t>(xs_bytes_b));
   consumers_sync();
   trace_mark(p.trace, 4);
   if (!consume_range<NCB, false, FAST>(ring, p.dn, b0, b1, xs, fxB, p.ntok, p.out, p.status))
@@ -1007,11 +1018,12 @@ __device__ void push_down(const StackParams& p, uint32_t par, uint32_t row0, uin
 }
 
 // TP = true: one rank of a tensor-parallel stack (see StackParams).  Phase B
-// writes this rank's partial down projection into its own exchange slot,
-// pushes it to every peer and meets all ranks' CTAs at a peer barrier; the
-// next glue sums the ranks' slots in rank order.  The slots alternate
-// between two parities by the global count of peer barriers, so a rank that
-// runs ahead writes the other parity from the one its peers still read.
+// writes this rank's partial down projection into its own exchange slot and
+// pushes it to every peer; after the rank's grid barrier the ranks meet in
+// peer_exchange, and the next glue sums the ranks' slots in rank order.  The
+// slots alternate between two parities by the global count of exchanges, so
+// a rank that runs ahead writes the other parity from the one its peers
+// still read.
 template <int NT, bool FAST, bool TP>
 __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const __grid_constant__ StackParams p) {
   constexpr int NC = NT;  // bf16 activations: one fragment column per token
@@ -1025,7 +1037,7 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const __gr
   const Partition ptB = Partition::make(p.dn.RT, p.dn.KT, gridDim.x);
   Shape::init_barriers(smem, p.nst);
   const unsigned long long bar_base = threadIdx.x == 0 ? grid_base(p.bar, gridDim.x) : 0ull;
-  if (TP && threadIdx.x == 0) xbase_s = peer_base(p.xr[p.rank], p.world, gridDim.x);
+  if (TP && threadIdx.x == 0) xbase_s = peer_base(p.xr[p.rank], p.world);
   if (lane == 0) {
     uint64_t a0, a1, b0, b1;
     ptA.warp_range(blockIdx.x, warp, a0, a1);
@@ -1072,7 +1084,7 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const __gr
     prow1 = static_cast<uint32_t>(c1 / p.dn.KT);
     if (prow1 < prow0) prow1 = prow0;
     xbase = xbase_s;
-    xpar0 = static_cast<uint32_t>(xbase / (static_cast<unsigned long long>(p.world) * gridDim.x)) & 1u;
+    xpar0 = static_cast<uint32_t>(xbase / p.world) & 1u;
   }
   const uint32_t* my = wk[warp];
   ConsumerRing<kUnitsPerStage, StackWork> ring;
@@ -1114,9 +1126,7 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const __gr
         glue<true, true>(p.ntok, p.H, p.eps, Bf16In{xres}, down_in(l - 1), Bf16Out{xres}, xn, red, tr);
       }
     } else {
-      const uint32_t xs_b = static_cast<uint32_t>(frag_bytes(p.dn.KT, NC));
-      for (uint32_t o = threadIdx.x * 16; o < xs_b; o += NTHR * 16)
-        *reinterpret_cast<uint4*>(xs + o) = __ldcg(reinterpret_cast<const uint4*>(p.act + o));
+      stage_from_l2(xs, p.act, static_cast<uint32_t>(frag_bytes(p.dn.KT, NC)));
     }
     consumers_sync();
     trace_mark(tr, B ? 4 : 1);
@@ -1140,11 +1150,8 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const __gr
       consumers_sync();
       trace_mark(tr, B ? 5 : 2);
     }
-    bool bar_ok;
-    if (TP && B)
-      bar_ok = peer_barrier_epoch(p.xr, p.world, p.rank, gridDim.x, xbase, l + 1, p.status);
-    else
-      bar_ok = grid_barrier_epoch(p.bar, gridDim.x, bar_base, TP ? l + 1 : i + 1, p.status);
+    bool bar_ok = grid_barrier_epoch(p.bar, gridDim.x, bar_base, i + 1, p.status);
+    if (TP && B && bar_ok) bar_ok = peer_exchange(p.xr, p.world, p.rank, xbase, l + 1, p.status);
     if (!bar_ok || !consumers_and(ok)) {
       ring.drain();
       return;
