@@ -54,6 +54,7 @@ SIGNATURES = {
     "alv_ffn_stack_finalize": (_i, [_vp, _i, _i, _vp, _vp, _vp, _vp]),
     "alv_ffn_stack_create": (_i, [_vp, _c.POINTER(_u32), _i, _c.POINTER(_u32)]),
     "alv_ffn_stack_run": (_i, [_vp, _u32, _i, _vp, _vp, _vp]),
+    "alv_activation": (_i, [_vp, _i, _i, _vp, _vp, _vp, _vp]),
     "alv_ffn_stack_exchange": (_i, [_vp, _u32, _i, _vp]),
     "alv_ffn_stack_connect": (_i, [_vp, _u32, _i, _i, _vp]),
     "alv_run_gemv": (_i, [_vp, _u32, _i, _vp, _i, _vp, _i]),

@@ -1085,6 +1085,20 @@ extern "C" int alv_ffn_stack_run(alv_ctx* ctx, alv_handle h, int ntok, const uin
   return p.gu.fast ? launch_stack_f<true, false>(ctx, p, nt, st) : launch_stack_f<false, false>(ctx, p, nt, st);
 }
 
+extern "C" int alv_activation(alv_ctx* ctx, int act, int n, const uint16_t* gate, const uint16_t* up, uint16_t* out,
+                              void* stream) {
+  if (!ctx || n < 0 || (n && (!gate || !up || !out)) || (act != ALV_ACT_GELU && act != ALV_ACT_SILU))
+    return fail(ctx, ALV_ERR_ARG, "activation: bad argument");
+  if (!n) return ALV_OK;
+  int rc = set_device(ctx);
+  if (rc) return rc;
+  const uint32_t threads = 256, blocks = (static_cast<uint32_t>(n) + threads - 1) / threads;
+  activation_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(act == ALV_ACT_GELU ? 0 : 1,
+                                                                              static_cast<uint32_t>(n), gate, up, out);
+  ALV_CUDA(ctx, cudaGetLastError());
+  return ALV_OK;
+}
+
 extern "C" int alv_ffn_stack_exchange(alv_ctx* ctx, alv_handle h, int world, void* blob) {
   if (!ctx || !blob) return fail(ctx, ALV_ERR_ARG, "ffn_stack_exchange: bad argument");
   Weight* w = get_weight(ctx, h, 3);

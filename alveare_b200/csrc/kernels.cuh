@@ -300,11 +300,45 @@ __device__ __forceinline__ float geglu_ref(float g, float u) {
   return static_cast<float>(gelu * static_cast<double>(u));
 }
 
+// A float whose bf16 rounding equals that of geglu_ref(g, u), mostly in
+// float32: 0.5 g (1 + tanh z) = g / (1 + exp(-2z)), z = sqrt(2/pi) * inner,
+// has no cancellation and stays within ~1e-6 relative of the float64 value
+// for |z| <= 9 (expf: 2 ulp; the rest: four float32 roundings).  That result
+// is kept when it lies more than 256 float32 ulps (1.5e-5 relative) from a
+// bf16 rounding midpoint, so the float64 value and its float32 rounding fall
+// on the same side of every midpoint; otherwise (and for |z| > 9, where
+// float64 1 + tanh(z) itself cancels, or a zero / non-normal result) it
+// returns geglu_ref.
+__device__ __forceinline__ float geglu_act(float g, float u) {
+  const float g3 = __fmul_rn(__fmul_rn(g, g), g);
+  const float inner = __fadd_rn(g, __fmul_rn(0x1.6e4e26p-5f, g3));
+  const float z = 0x1.988454p-1f * inner;
+  if (fabsf(z) <= 9.0f) {
+    const float y = __fdiv_rn(g, 1.0f + expf(-2.0f * z)) * u;
+    const uint32_t b = __float_as_uint(y), e = (b >> 23) & 0xFFu;
+    const int lo = static_cast<int>(b & 0xFFFFu) - 0x8000;
+    if (e != 0u && e != 0xFFu && (lo > 256 || lo < -256)) return y;
+  }
+  return geglu_ref(g, u);
+}
+
 // SwiGLU as runtime/py/model.py:857-859 (float32 throughout).
 __device__ __forceinline__ float swiglu_ref(float g, float u) {
   const float e = static_cast<float>(exp(-static_cast<double>(g)));  // correctly rounded expf
   const float s = __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
   return __fmul_rn(__fmul_rn(g, s), u);
+}
+
+// act = bf16(act_fn(gate) * up) elementwise, with the FFN epilogue's own
+// functions (the reference's activation step,
+// kernels/ffn_fused/ffn_compute_activation.cc:17-64, with model.py's exact
+// formulas): gate, up, out bf16 bits.
+__global__ void activation_kernel(int fn, uint32_t n, const uint16_t* __restrict__ gate,
+                                  const uint16_t* __restrict__ up, uint16_t* __restrict__ out) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float g = bf16_bits_to_f32(gate[i]), u = bf16_bits_to_f32(up[i]);
+  out[i] = bf16_bits_rn(fn == 0 ? geglu_act(g, u) : swiglu_ref(g, u));
 }
 
 // Byte offset of value (column n, k) in the B-fragment layout (stage_frags).
@@ -324,7 +358,7 @@ struct GateUpEpi {  // tile rows 0-7 gate, 8-15 up of the same 8 intermediate in
     const uint32_t i = r * 8 + g;
     if (i >= I) return;
     const float gate = bf16_round(vg * sm), up = bf16_round(vg8 * sm);
-    const float a = fn == 0 ? geglu_ref(gate, up) : swiglu_ref(gate, up);
+    const float a = fn == 0 ? geglu_act(gate, up) : swiglu_ref(gate, up);
     *reinterpret_cast<uint16_t*>(act + frag_offset(ncb, static_cast<uint32_t>(tok), i)) = bf16_bits_rn(a);
   }
 };

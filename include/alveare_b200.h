@@ -169,6 +169,14 @@ int alv_ffn_stack_create(alv_ctx* ctx, const alv_handle* layers, int n, alv_hand
 int alv_ffn_stack_run(alv_ctx* ctx, alv_handle stack, int ntok, const uint16_t* x_in, uint16_t* out,
                       void* stream);
 
+/* act = bf16(act_fn(gate) * up) for n bf16 values (device buffers), with
+ * the FFN kernels' own epilogue: GeGLU / SwiGLU exactly as
+ * runtime/py/model.py:690-693 / :857-859 evaluate them in numpy.  Replaces
+ * the reference's activation step kernel
+ * (kernels/ffn_fused/ffn_compute_activation.cc:17-64). */
+int alv_activation(alv_ctx* ctx, int act, int n, const uint16_t* gate, const uint16_t* up, uint16_t* out,
+                   void* stream);
+
 /* Tensor-parallel FFN stack over the GPUs of one node, one process per GPU.
  * The reference splits each FFN's intermediate dimension over compute tiles
  * and sums the partial down projections on the host

@@ -1,0 +1,46 @@
+"""The FFN activation epilogue (alv_activation, the same device functions
+the FFN kernels apply) against the oracle's restatement of numpy's GeGLU /
+SwiGLU (runtime/py/model.py:690-693, :857-859), bit for bit on bf16: every
+bf16 gate value with |g| <= 20 (subnormals and zeros included) against
+several up vectors.  GeGLU runs a float32 fast path that must fall back to
+float64 wherever the bf16 rounding could differ."""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+from alveare_b200 import _lib  # noqa: E402
+from oracle import q4  # noqa: E402
+
+
+def all_bf16_upto(limit: float) -> np.ndarray:
+    pos = np.arange(0, 0x7F80, dtype=np.uint16)
+    vals = q4.bits_to_f32(pos)
+    pos = pos[np.abs(vals) <= limit]
+    return np.concatenate([pos, pos | np.uint16(0x8000)])
+
+
+def run(act: int, g_bits: np.ndarray, u_bits: np.ndarray) -> np.ndarray:
+    ctx = _lib.context(0)
+    g = torch.from_numpy(g_bits.view(np.int16)).cuda()
+    u = torch.from_numpy(u_bits.view(np.int16)).cuda()
+    out = torch.empty_like(g)
+    ctx.check(ctx.lib.alv_activation(ctx.ptr, act, g.numel(), g.data_ptr(), u.data_ptr(), out.data_ptr(),
+                                     torch.cuda.current_stream().cuda_stream), "alv_activation")
+    ctx.sync_status()
+    return out.cpu().numpy().view(np.uint16)
+
+
+@pytest.mark.parametrize("act,ref", [(_lib.ACT_GELU, q4.act_geglu), (_lib.ACT_SILU, q4.act_swiglu)])
+def test_activation_bit_exact_over_all_bf16_gates(act, ref):
+    g_bits = all_bf16_upto(20.0)
+    rng = np.random.default_rng(3)
+    ups = [rng.normal(0, 1, g_bits.size), rng.normal(0, 30, g_bits.size),
+           np.full(g_bits.size, 1.0), np.full(g_bits.size, -0.3125)]
+    for u in ups:
+        u_bits = q4.bf16_bits(q4.to_bf16(u.astype(np.float32)))
+        got = run(act, g_bits, u_bits)
+        want = q4.bf16_bits(ref(q4.bits_to_f32(g_bits), q4.bits_to_f32(u_bits)))
+        bad = np.flatnonzero(got != want)
+        assert bad.size == 0, f"{bad.size} mismatches, first g={q4.bits_to_f32(g_bits[bad[:4]])}"
