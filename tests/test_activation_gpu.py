@@ -9,7 +9,10 @@ One exception, in the oracle rather than the kernel: for z = sqrt(2/pi) *
 (g + 0.044715 g^3) < -10, float64 1 + tanh(z) cancels to < 4e-9, and numpy's
 vectorized tanh is not correctly rounded there (at g = -6.8125 it is one
 double step off the correctly rounded value, which the GPU returns), so such
-results (below 1e-8 |g u|) are held to two 2^-53 steps of 1 + tanh(z)."""
+results (below 1e-8 |g u|) are held to two 2^-53 steps of 1 + tanh(z).
+Likewise numpy's float32 exp in SwiGLU is not correctly rounded at every
+point; where it differs from the correctly rounded exp the GPU uses, one bf16
+step is allowed."""
 import numpy as np
 import pytest
 
@@ -57,5 +60,15 @@ def test_activation_bit_exact_over_all_bf16_gates(act, ref):
             near = np.abs(0.5 * g.astype(np.float64) * uf) * 2.0 ** -52
             assert np.all(err[diff & cancel] <= near[diff & cancel])
             diff &= ~cancel
+        else:
+            # numpy's vectorized float32 exp is not correctly rounded everywhere
+            # (one ulp off at g = 1.04e-7, for one); the GPU's is.  Where the
+            # two exps differ, allow one bf16 step.
+            e_np = np.exp(-g)
+            e_cr = np.exp(-g.astype(np.float64)).astype(np.float32)
+            off = e_np != e_cr
+            step = np.abs(got.astype(np.int32) - want.astype(np.int32))
+            assert np.all(step[diff & off] <= 1)
+            diff &= ~off
         bad = np.flatnonzero(diff)
         assert bad.size == 0, f"{bad.size} mismatches, first g={g[bad[:4]]}"
