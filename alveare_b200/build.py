@@ -1,10 +1,12 @@
 """Build the in-tree native library ``alveare_b200/libalveare_b200.so`` for sm_100a.
 
-    python -m alveare_b200.build
+    python -m alveare_b200.build [--force] [-v]
 
-The library is compiled straight from ``alveare_b200/csrc`` with nvcc
-(``-gencode arch=compute_100a,code=sm_100a``), statically linked against the
-CUDA runtime so it does not depend on which libcudart torch brought along.
+Every ``alveare_b200/csrc/*.cu`` translation unit is compiled with nvcc
+(``-gencode arch=compute_100a,code=sm_100a``) in parallel, then linked into
+one shared library, statically linked against the CUDA runtime so it does not
+depend on which libcudart torch brought along.  Object files go to
+``alveare_b200/_build/`` (not committed).
 """
 from __future__ import annotations
 
@@ -12,11 +14,14 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
+OBJ = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libalveare_b200.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC"]
 
 
 def nvcc() -> str:
@@ -26,28 +31,41 @@ def nvcc() -> str:
     return cand
 
 
+def units() -> list[str]:
+    return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cu"))
+
+
 def sources() -> list[str]:
-    return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cu", ".cuh")))
+    hdr = os.path.join(os.path.dirname(HERE), "include", "alveare_b200.h")
+    return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cu", ".cuh", ".h"))) + [hdr]
 
 
 def needs_build() -> bool:
     if not os.path.exists(LIB):
         return True
     t = os.path.getmtime(LIB)
-    hdr = os.path.join(os.path.dirname(HERE), "include", "alveare_b200.h")
-    return any(os.path.getmtime(s) > t for s in sources() + [hdr])
+    return any(os.path.getmtime(s) > t for s in sources())
+
+
+def _compile(src: str, verbose: bool) -> str:
+    obj = os.path.join(OBJ, os.path.basename(src)[:-3] + ".o")
+    cmd = [nvcc(), *ARCH, *FLAGS, "-c", "-o", obj, src]
+    if verbose:
+        cmd.insert(1, "-Xptxas=-v")
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    return obj
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
     if not force and not needs_build():
         return LIB
+    os.makedirs(OBJ, exist_ok=True)
+    srcs = units()
+    with ThreadPoolExecutor(max_workers=max(1, min(len(srcs), os.cpu_count() or 1))) as ex:
+        objs = list(ex.map(lambda s: _compile(s, verbose), srcs))
     tmp = LIB + ".tmp"
-    cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
-           "-cudart", "static", "-o", tmp, os.path.join(CSRC, "alveare.cu")]
-    if verbose:
-        cmd.insert(1, "-Xptxas=-v")
-        print(" ".join(cmd), flush=True)
-    subprocess.run(cmd, check=True)
+    subprocess.run([nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", tmp, *objs], check=True)
     os.replace(tmp, LIB)
     return LIB
 

@@ -101,7 +101,7 @@ __device__ __forceinline__ bool mbar_try_wait_sleep_s(uint32_t bar, uint32_t par
       : "memory");
   return ok != 0;
 }
-__device__ __noinline__ bool mbar_wait_bounded_slow(uint32_t bar, uint32_t parity) {
+static __device__ __noinline__ bool mbar_wait_bounded_slow(uint32_t bar, uint32_t parity) {
   const unsigned long long t0 = globaltimer_ns();
   while (true) {
     if (mbar_try_wait_sleep_s(bar, parity, 100000u)) return true;  // sleep up to 0.1 ms

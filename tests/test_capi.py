@@ -41,7 +41,7 @@ def test_signature_table_has_no_extra_entries():
 
 
 def test_version_and_null_handling(lib):
-    assert lib.alv_version() == 100
+    assert lib.alv_version() == 200
     assert lib.alv_last_error(None) == b"null context"
     assert lib.alv_ctx_destroy(None) == 1          # ALV_ERR_ARG
     assert lib.alv_sync_status(None, None) == 1
