@@ -62,6 +62,8 @@ SIGNATURES = {
     "alv_gemv_noalloc": (_i, [_vp, _u32, _i, _vp, _i, _vp, _i, _vp]),
     "alv_gemm": (_i, [_vp, _u32, _i, _vp, _vp, _i, _vp]),
     "alv_set_trace": (_i, [_vp, _vp]),
+    "alv_ctx_info": (_i, [_vp, _c.POINTER(_c.c_int64)]),
+    "alv_ffn_stack_set_probe": (_i, [_vp, _u32, _vp]),
 }
 
 _lock = threading.Lock()
@@ -113,6 +115,13 @@ class Context:
 
     def sync_status(self, stream: int | None = None) -> None:
         self.check(self.lib.alv_sync_status(self.ptr, stream), "alv_sync_status")
+
+    def info(self) -> dict:
+        """alv_ctx_info as a dict."""
+        out = (_c.c_int64 * 8)()
+        self.check(self.lib.alv_ctx_info(self.ptr, out), "alv_ctx_info")
+        keys = ("device", "num_sms", "scratch_bytes", "io_bytes", "allocs", "handles")
+        return dict(zip(keys, list(out)[:6]))
 
     def close(self) -> None:
         if self.ptr:

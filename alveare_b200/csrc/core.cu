@@ -32,7 +32,7 @@ __global__ void __launch_bounds__(kConsumerWarps * 32, 1)
 
 int ensure_scratch(alv_ctx* ctx, size_t work_bytes) {
   if (!ctx->sync) {
-    ALV_CUDA(ctx, cudaMalloc(&ctx->sync, kSyncBytes));
+    ALV_CUDA(ctx, dev_alloc(ctx, &ctx->sync, kSyncBytes));
     ALV_CUDA(ctx, cudaMemset(ctx->sync, 0, kSyncBytes));
   }
   if (ctx->scratch && ctx->scratch_bytes >= work_bytes) return ALV_OK;
@@ -40,7 +40,7 @@ int ensure_scratch(alv_ctx* ctx, size_t work_bytes) {
   if (ctx->scratch) ctx->retired.push_back(ctx->scratch);
   ctx->scratch = nullptr;
   const size_t bytes = std::max(work_bytes, static_cast<size_t>(8) << 20);
-  ALV_CUDA(ctx, cudaMalloc(&ctx->scratch, bytes));
+  ALV_CUDA(ctx, dev_alloc(ctx, &ctx->scratch, bytes));
   ALV_CUDA(ctx, cudaMemset(ctx->scratch, 0, bytes));
   ctx->scratch_bytes = bytes;
   return ALV_OK;
@@ -99,7 +99,7 @@ int io_buffers(alv_ctx* ctx, size_t bytes) {
   if (ctx->io && ctx->io_bytes >= bytes) return ALV_OK;
   if (ctx->io) ctx->retired.push_back(ctx->io);
   ctx->io = nullptr;
-  ALV_CUDA(ctx, cudaMalloc(&ctx->io, bytes));
+  ALV_CUDA(ctx, dev_alloc(ctx, &ctx->io, bytes));
   ctx->io_bytes = bytes;
   return ALV_OK;
 }
@@ -114,7 +114,7 @@ struct Survey {
 
 int survey_mat(alv_ctx* ctx, const RepackSrc& s, Survey* out) {
   int* info = nullptr;
-  ALV_CUDA(ctx, cudaMalloc(&info, 3 * sizeof(int)));
+  ALV_CUDA(ctx, dev_alloc(ctx, &info, 3 * sizeof(int)));
   const int init[3] = {INT_MIN, INT_MAX, 0};
   ALV_CUDA(ctx, cudaMemcpyAsync(info, init, sizeof(init), cudaMemcpyHostToDevice, ctx->stream));
   const uint64_t nblk = static_cast<uint64_t>(s.RT) * 16 * (s.K / 32);
@@ -145,7 +145,7 @@ int repack_mat(alv_ctx* ctx, const RepackSrc& s, const Survey& sv, uint32_t rows
   const uint64_t nunits = static_cast<uint64_t>(s.RT) * s.KT;
   Mat m;
   m.bytes = nunits * kUnitBytes;
-  ALV_CUDA(ctx, cudaMalloc(&m.dev, std::max<size_t>(m.bytes, 16)));
+  ALV_CUDA(ctx, dev_alloc(ctx, &m.dev, std::max<size_t>(m.bytes, 16)));
   if (nunits) {
     const uint64_t nwords = nunits * 144;
     q4_repack_kernel<<<static_cast<unsigned>((nwords + 255) / 256), 256, 0, ctx->stream>>>(
@@ -180,7 +180,7 @@ int stage_source(alv_ctx* ctx, const void* src, size_t bytes, int on_device, con
     return ALV_OK;
   }
   uint8_t* d = nullptr;
-  ALV_CUDA(ctx, cudaMalloc(&d, std::max<size_t>(bytes, 16)));
+  ALV_CUDA(ctx, dev_alloc(ctx, &d, std::max<size_t>(bytes, 16)));
   ALV_CUDA(ctx, cudaMemcpy(d, src, bytes, cudaMemcpyHostToDevice));
   *dev = d;
   *owned = d;
@@ -233,6 +233,18 @@ int alv_ctx_destroy(alv_ctx* ctx) {
   for (void* q : ctx->retired) cudaFree(q);
   cudaStreamDestroy(ctx->stream);
   delete ctx;
+  return ALV_OK;
+}
+
+int alv_ctx_info(alv_ctx* ctx, int64_t* info) {
+  if (!ctx || !info) return ALV_ERR_ARG;
+  info[0] = ctx->device;
+  info[1] = ctx->num_sms;
+  info[2] = static_cast<int64_t>(ctx->scratch_bytes);
+  info[3] = static_cast<int64_t>(ctx->io_bytes);
+  info[4] = ctx->allocs;
+  info[5] = static_cast<int64_t>(ctx->weights.size());
+  info[6] = info[7] = 0;
   return ALV_OK;
 }
 
@@ -436,7 +448,7 @@ int alv_weight_dequantize(alv_ctx* ctx, alv_handle h, int which, uint16_t* out, 
     // temporary (2*I rows) and gather the requested half.
     const uint32_t rows_all = m->m.RT * 16;
     uint16_t* tmp = nullptr;
-    ALV_CUDA(ctx, cudaMalloc(&tmp, static_cast<size_t>(rows_all) * K * 2));
+    ALV_CUDA(ctx, dev_alloc(ctx, &tmp, static_cast<size_t>(rows_all) * K * 2));
     q4_dequant_kernel<<<static_cast<unsigned>((nthreads + 255) / 256), 256, 0, st>>>(m->m, rows_all, K, tmp);
     ALV_CUDA(ctx, cudaGetLastError());
     for (uint32_t i = 0; i < rows; ++i) {

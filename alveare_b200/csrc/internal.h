@@ -53,6 +53,7 @@ struct Weight {
   uint32_t xslot = 0, xws_off = 0;
   uint8_t* xr[kMaxRanksHost] = {};
   unsigned char blob[ALV_IPC_BLOB_BYTES] = {};
+  float* probe = nullptr;  // kind 3: optional fp32 copy of the last layer's down projection
   // kind 4: decode model state (owned by decode.cu)
   void* model = nullptr;
   void (*model_free)(void*) = nullptr;
@@ -73,6 +74,7 @@ struct alv_ctx {
   size_t io_bytes = 0;
   cudaStream_t stream = nullptr;                      // internal stream (loads, host calls)
   unsigned long long* trace = nullptr;                // optional FFN phase timestamps
+  int64_t allocs = 0;                                 // device allocations made through this context
 };
 
 namespace alv {
@@ -88,6 +90,14 @@ inline int fail(alv_ctx* ctx, int code, const std::string& msg) {
     if (e_ != cudaSuccess)                                                               \
       return ::alv::fail((ctx), ALV_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
   } while (0)
+
+// Every device allocation of the library goes through here (counted per
+// context, reported by alv_ctx_info).
+template <class T>
+cudaError_t dev_alloc(alv_ctx* ctx, T** p, size_t bytes) {
+  ++ctx->allocs;
+  return cudaMalloc(reinterpret_cast<void**>(p), bytes);
+}
 
 inline int set_device(alv_ctx* ctx) {
   ALV_CUDA(ctx, cudaSetDevice(ctx->device));

@@ -759,6 +759,7 @@ struct StackParams {
   uint32_t* status;
   uint32_t nst;
   unsigned long long* trace;  // optional: phase stamps of layer 1
+  float* probe;               // optional: [ntok][H] fp32 down projection of the last layer
   // Tensor parallelism (ffn_stack_kernel<..., TP = true>): rank `rank` of
   // `world` holds an I-slice of every layer.  xr[q] is rank q's exchange
   // region as mapped on this GPU (xr[rank] is this GPU's own):
@@ -839,6 +840,20 @@ inline __device__ void push_down(const StackParams& p, uint32_t par, uint32_t ro
     const float v = __ldcg(src + off);
     for (uint32_t q = 0; q < p.world; ++q)
       if (q != p.rank) xslot_ptr(p, q, par, p.rank)[off] = v;
+  }
+}
+
+// The last layer's down projection as the final glue read it (fp32, summed
+// over CTAs and, with tensor parallelism, over ranks): a test probe.
+template <class DL>
+__device__ void write_probe(float* probe, int ntok, uint32_t H, const DL& dl) {
+  const uint32_t n = static_cast<uint32_t>(ntok) * H;
+  for (uint32_t e = threadIdx.x; e < n; e += kConsumerWarps * 32) {
+    const uint32_t tok = e / H, h = e - tok * H;
+    float a, b;
+    uint32_t how;
+    dl.load(tok, h, e, a, b, how);
+    probe[e] = dl.combine(a, b, how);
   }
 }
 
@@ -987,10 +1002,13 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const __gr
     float* red = reinterpret_cast<float*>(smem + base_smem_bytes(p.nst, p.ntok) +
                                           stack_xs_region(p.gu.KT, p.dn.KT, NC, p.H, p.ntok));
     const Bf16In xl{reinterpret_cast<uint16_t*>(red + 32)};
-    if constexpr (TP)
+    if constexpr (TP) {
       glue<false, true>(p.ntok, p.H, p.eps, xl, down_in_x(p.L - 1), Bf16Out{p.out}, XnOut{}, red);
-    else
+      if (p.probe) write_probe(p.probe, p.ntok, p.H, down_in_x(p.L - 1));
+    } else {
       glue<false, true>(p.ntok, p.H, p.eps, xl, down_in(p.L - 1), Bf16Out{p.out}, XnOut{}, red);
+      if (p.probe) write_probe(p.probe, p.ntok, p.H, down_in(p.L - 1));
+    }
   }
 }
 

@@ -107,9 +107,9 @@ extern "C" int alv_ffn_stack_create(alv_ctx* ctx, const alv_handle* layers, int 
   s->act = w0->act;
   s->layers.assign(layers, layers + n);
   const StackLayout lo = stack_layout(ctx, s.get());
-  ALV_CUDA(ctx, cudaMalloc(&s->layers_dev, sizeof(LayerW) * lw.size()));
+  ALV_CUDA(ctx, dev_alloc(ctx, &s->layers_dev, sizeof(LayerW) * lw.size()));
   ALV_CUDA(ctx, cudaMemcpy(s->layers_dev, lw.data(), sizeof(LayerW) * lw.size(), cudaMemcpyHostToDevice));
-  ALV_CUDA(ctx, cudaMalloc(&s->ws, lo.total));
+  ALV_CUDA(ctx, dev_alloc(ctx, &s->ws, lo.total));
   ALV_CUDA(ctx, cudaMemset(s->ws, 0, lo.total));
   s->ws_bytes = lo.total;
   *out = add_weight(ctx, std::move(s));
@@ -157,6 +157,7 @@ extern "C" int alv_ffn_stack_run(alv_ctx* ctx, alv_handle h, int ntok, const uin
   p.bar = reinterpret_cast<GridBar*>(w->ws + 256);
   p.status = reinterpret_cast<uint32_t*>(w->ws);
   p.trace = ctx->trace;
+  p.probe = w->probe;
   const uint32_t nt = pow2_ceil(static_cast<uint32_t>(ntok));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (tp) {
@@ -181,7 +182,7 @@ extern "C" int alv_ffn_stack_exchange(alv_ctx* ctx, alv_handle h, int world, voi
   if (rc) return rc;
   exchange_shape(ctx, w, &w->xslot, &w->xws_off);
   const size_t bytes = kXHeader + static_cast<size_t>(2) * world * w->xslot * 4;
-  ALV_CUDA(ctx, cudaMalloc(&w->xlocal, bytes));
+  ALV_CUDA(ctx, dev_alloc(ctx, &w->xlocal, bytes));
   ALV_CUDA(ctx, cudaMemset(w->xlocal, 0, bytes));
   ALV_CUDA(ctx, cudaDeviceSynchronize());
   cudaIpcMemHandle_t ih;
@@ -260,5 +261,13 @@ extern "C" int alv_ffn_stack_connect(alv_ctx* ctx, alv_handle h, int rank, int w
   }
   w->rank = rank;
   w->connected = true;
+  return ALV_OK;
+}
+
+extern "C" int alv_ffn_stack_set_probe(alv_ctx* ctx, alv_handle h, float* down_last) {
+  if (!ctx) return ALV_ERR_ARG;
+  Weight* w = get_weight(ctx, h, 3);
+  if (!w) return fail(ctx, ALV_ERR_HANDLE, "ffn_stack_set_probe: invalid handle (not an ffn stack)");
+  w->probe = down_last;
   return ALV_OK;
 }

@@ -13,9 +13,13 @@ reference's NPU operators, so ``runtime/py`` can switch by import:
 Tensors are torch CUDA tensors (stream-ordered on the current stream) or host
 numpy arrays (synchronous copy in / copy out, like the reference's
 ``_sync_to_device``).  ``m``, ``k_tile`` and ``m_I`` are NPU tiling knobs;
-they are accepted and ignored.  A raw ``W_combined`` buffer is repacked on
-every call, like the reference's non-resident path (model.py:291-295, 355-356);
-register it once with :class:`Q4Weight` for the resident path.
+they are accepted and ignored.  A raw ``W_combined`` buffer is repacked into
+the GPU layout on its first use and the resident copy is reused while the
+same buffer (same object, address and size, and for a torch tensor the same
+version counter) comes back, the way the reference keeps its weights resident
+(model.py:41-53); :class:`Q4Weight` registers one explicitly, and
+:func:`clear_weight_cache` drops the cached copies (call it after changing a
+raw buffer in place by other means than torch).
 """
 from __future__ import annotations
 
@@ -242,13 +246,41 @@ def _run(ctx, kind: str, handle: int, ntok: int, X, Y, device: int) -> None:
             Y.copy_(torch.from_numpy(ya.view(np.int16)).view(torch.bfloat16))
 
 
+# Raw packed buffers seen by the operators -> their resident Q4Weight.  The
+# source object is held, so its address cannot be reused by another buffer
+# while the entry lives.
+_WEIGHT_CACHE: dict = {}
+
+
+def _buffer_key(W, N: int, K: int, device):
+    if _is_torch(W):
+        dev = W.device.index if W.is_cuda else -1
+        return ("torch", dev, W.data_ptr(), W.numel() * W.element_size(), N, K, device), W._version
+    a = np.asarray(W)
+    return ("host", -1, a.__array_interface__["data"][0], a.nbytes, N, K, device), 0
+
+
+def clear_weight_cache() -> None:
+    """Free every resident copy made for a raw W_combined buffer."""
+    for _, _, w in list(_WEIGHT_CACHE.values()):
+        w.free()
+    _WEIGHT_CACHE.clear()
+
+
 def _as_weight(W, N, K, device):
     if isinstance(W, Q4Weight):
         if W.N != N or W.K != K:
             raise ValueError(f"weight is ({W.N}, {W.K}), call asked for ({N}, {K})")
-        return W, False
-    w = Q4Weight(W if len(getattr(W, "shape", ())) == 2 else W, N=N, K=K, device=device)
-    return w, True
+        return W
+    key, version = _buffer_key(W, N, K, device)
+    hit = _WEIGHT_CACHE.get(key)
+    if hit is not None and hit[0] is W and hit[1] == version:
+        return hit[2]
+    if hit is not None:
+        hit[2].free()
+    w = Q4Weight(W, N=N, K=K, device=device)
+    _WEIGHT_CACHE[key] = (W, version, w)
+    return w
 
 
 # ---------------------------------------------------------------------------
@@ -258,18 +290,12 @@ def gemv_q_npu(W_combined, X, Y, *, N: int, K: int, m: int = 32, k_tile: int = 2
     """Y[N] = W[N, K] @ X[K] for the Q4 matrix W (kernels/gemv_q/gemv_q.py:33-43).
     Y is written in place (fp32 or bf16)."""
     device = _device_of(X, Y, W_combined)
-    w, temp = _as_weight(W_combined, N, K, device)
-    try:
-        if int(np.prod(X.shape)) < K or int(np.prod(Y.shape)) < N:
-            raise ValueError("X or Y too small for (N, K)")
-        Xv = X[:K] if X.shape[0] > K and len(X.shape) == 1 else X
-        Yv = Y[:N] if Y.shape[0] > N and len(Y.shape) == 1 else Y
-        _run(w.ctx, "gemv", w.handle, 1, Xv, Yv, w.device)
-    finally:
-        if temp:
-            if _is_torch(X) and X.is_cuda:
-                torch.cuda.current_stream(w.device).synchronize()
-            w.free()
+    w = _as_weight(W_combined, N, K, device)
+    if int(np.prod(X.shape)) < K or int(np.prod(Y.shape)) < N:
+        raise ValueError("X or Y too small for (N, K)")
+    Xv = X[:K] if X.shape[0] > K and len(X.shape) == 1 else X
+    Yv = Y[:N] if Y.shape[0] > N and len(Y.shape) == 1 else Y
+    _run(w.ctx, "gemv", w.handle, 1, Xv, Yv, w.device)
 
 
 # Batches above this many bf16 tokens run on the tcgen05 prefill kernel; the
@@ -316,26 +342,20 @@ def gemm_q_npu(W_combined, X, Y, *, B: int, N: int, K: int, m: int = 32, k_tile:
     (tcgen05); smaller ones (and fp32 X) are processed by the streaming gemv
     in slices of 16 (8 for fp32) tokens."""
     device = _device_of(X, Y, W_combined)
-    w, temp = _as_weight(W_combined, N, K, device)
-    try:
-        Xv = X.reshape(B, K) if not (len(X.shape) == 2 and tuple(X.shape) == (B, K)) else X
-        Yv = Y.reshape(B, N) if not (len(Y.shape) == 2 and tuple(Y.shape) == (B, N)) else Y
-        if _dtype_code(X) == BF16 and B >= GEMM_TC_MIN_TOKENS:
-            _gemm_tc(w, B, Xv, Yv)
-            return
-        step = 16 if _dtype_code(X) == BF16 else 8
-        for b0 in range(0, B, step):
-            b1 = min(B, b0 + step)
-            xs, ys = Xv[b0:b1], Yv[b0:b1]
-            if _is_torch(ys) or not ys.flags["C_CONTIGUOUS"]:
-                _run(w.ctx, "gemv", w.handle, b1 - b0, xs, ys, w.device)
-            else:
-                _run(w.ctx, "gemv", w.handle, b1 - b0, np.ascontiguousarray(xs), ys, w.device)
-    finally:
-        if temp:
-            if _is_torch(X) and X.is_cuda:
-                torch.cuda.current_stream(w.device).synchronize()
-            w.free()
+    w = _as_weight(W_combined, N, K, device)
+    Xv = X.reshape(B, K) if not (len(X.shape) == 2 and tuple(X.shape) == (B, K)) else X
+    Yv = Y.reshape(B, N) if not (len(Y.shape) == 2 and tuple(Y.shape) == (B, N)) else Y
+    if _dtype_code(X) == BF16 and B >= GEMM_TC_MIN_TOKENS:
+        _gemm_tc(w, B, Xv, Yv)
+        return
+    step = 16 if _dtype_code(X) == BF16 else 8
+    for b0 in range(0, B, step):
+        b1 = min(B, b0 + step)
+        xs, ys = Xv[b0:b1], Yv[b0:b1]
+        if _is_torch(ys) or not ys.flags["C_CONTIGUOUS"]:
+            _run(w.ctx, "gemv", w.handle, b1 - b0, xs, ys, w.device)
+        else:
+            _run(w.ctx, "gemv", w.handle, b1 - b0, np.ascontiguousarray(xs), ys, w.device)
 
 
 def pack_ffn_fused_weights(w_gate, w_up, w_down, H: int, I: int, m_I: int = 32, k_tile: int = 256,
@@ -351,17 +371,34 @@ def ffn_fused_npu(W_fused, X, Y_partial, *, H: int, I: int, m_I: int = 32, k_til
     """Fused FFN (kernels/ffn_fused/ffn_fused.py:28-39).  Writes the full
     y = Wd act(Wg x, Wu x) into row 0 of Y_partial and zeros the other rows,
     so summing Y_partial over its first axis (the reference host reduction)
-    returns y."""
+    returns y.
+
+    X may also hold a batch of 1..8 tokens, (B, H); Y_partial is then
+    (n_rows, B, H) with y in row 0, or (B, H)."""
     if not isinstance(W_fused, FusedFFNWeight):
         raise TypeError("W_fused must come from alveare_b200.pack_ffn_fused_weights")
     if W_fused.H != H or W_fused.I != I:
         raise ValueError(f"W_fused is (H={W_fused.H}, I={W_fused.I}), call asked for ({H}, {I})")
     W_fused.set_activation(activation)
+    if len(X.shape) == 2 and X.shape[0] > 1:
+        ntok = int(X.shape[0])
+        if not 1 <= ntok <= 8:
+            raise ValueError("ffn_fused_npu: a batch holds 1..8 tokens")
+        if tuple(Y_partial.shape[-2:]) != (ntok, H):
+            raise ValueError(f"Y_partial must end in ({ntok}, {H})")
+        if len(Y_partial.shape) == 3:
+            if Y_partial.shape[0] > 1:
+                Y_partial[1:] = 0
+            y0 = Y_partial[0]
+        else:
+            y0 = Y_partial
+        _run(W_fused.ctx, "ffn", W_fused.handle, ntok, X, y0, W_fused.device)
+        return
     Yp = Y_partial.reshape(-1, H) if Y_partial.shape[-1] != H or len(Y_partial.shape) != 2 else Y_partial
     if Yp.shape[0] > 1:
         Yp[1:] = 0
     y0 = Yp[0]
-    Xv = X[:H] if len(X.shape) == 1 and X.shape[0] > H else X
+    Xv = X.reshape(-1)[:H] if len(X.shape) == 2 else (X[:H] if X.shape[0] > H else X)
     _run(W_fused.ctx, "ffn", W_fused.handle, 1, Xv, y0, W_fused.device)
 
 

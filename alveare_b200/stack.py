@@ -63,6 +63,7 @@ class FFNStack:
         self.out = torch.zeros(H, dtype=torch.bfloat16, device=dev)
         self.graph = None
         self.stream = torch.cuda.Stream(device=dev)
+        self.probe = None
 
     @property
     def ctx(self):
@@ -83,9 +84,23 @@ class FFNStack:
             h = ctypes.c_uint32()
             ctx.check(ctx.lib.alv_ffn_stack_create(ctx.ptr, arr, n, ctypes.byref(h)), "alv_ffn_stack_create")
             self.stack_handle = h.value
+            if self.probe is not None:
+                ctx.check(ctx.lib.alv_ffn_stack_set_probe(ctx.ptr, self.stack_handle, self.probe.data_ptr()),
+                          "alv_ffn_stack_set_probe")
             if self.world > 1:
                 self._connect()
         return self.stack_handle
+
+    def set_probe(self, down_last: torch.Tensor) -> None:
+        """Make every later step of the one-launch stack also write the last
+        layer's down projection (H fp32, summed over the ranks) into
+        `down_last`, a CUDA tensor on this device.  A checking aid: call it
+        before the first step (a captured step keeps the pointer)."""
+        if self.stack_handle or self.graph is not None:
+            raise RuntimeError("FFNStack.set_probe: call before the first step")
+        if not (down_last.is_cuda and down_last.dtype == torch.float32 and down_last.numel() >= self.H):
+            raise ValueError("down_last must be a float32 CUDA tensor of at least H elements")
+        self.probe = down_last
 
     def _connect(self) -> None:
         """Map every rank's exchange region (collective over the process

@@ -83,7 +83,7 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -124,6 +124,15 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # CPU baseline (the C restatement of the reference's CPU path)
 # ---------------------------------------------------------------------------
+def host_threads() -> int:
+    """Host cores this process may run on.  Set explicitly for the OpenMP C
+    port: torchrun exports OMP_NUM_THREADS=1 to every rank."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover
+        return os.cpu_count() or 1
+
+
 def synthetic_cpu_layer(seed: int):
     """Random but well-formed packed Q4 matrices of the config-4 shapes (the
     CPU cost does not depend on the values)."""
@@ -148,7 +157,7 @@ def cpu_baseline(budget_s: float = 10.0) -> dict:
     import numpy as np
 
     from oracle import cpu
-    threads = cpu.max_threads()
+    threads = host_threads()
     g, u, d = synthetic_cpu_layer(0)
     x = np.random.default_rng(1).normal(0, 1, H).astype(np.float32)
     cpu.ffn_block(g, u, d, x, threads)  # warm-up
@@ -175,7 +184,7 @@ def run_reference(args) -> None:
     import numpy as np
 
     from oracle import cpu
-    threads = cpu.max_threads()
+    threads = host_threads()
     g, u, d = synthetic_cpu_layer(0)
     x = np.random.default_rng(1).normal(0, 1, H).astype(np.float32)
     layers_per_step = args.layers   # a whole decode step: every FFN half-block of the stack
@@ -199,6 +208,145 @@ def run_reference(args) -> None:
             "tokens_per_s": round(args.steps / dt, 4)}
     print(json.dumps(line), flush=True)
 
+
+
+# ---------------------------------------------------------------------------
+# the other configurations the metric names (1 GPU, rank 0)
+# ---------------------------------------------------------------------------
+def _time_graph(fn_launch, reps: int, calls_per_rep: int, stream) -> float:
+    """Capture fn_launch() (calls_per_rep kernel calls) into a CUDA graph,
+    replay it `reps` times after a warm-up; device microseconds per call."""
+    import torch
+    with torch.cuda.stream(stream):
+        fn_launch()                       # warm-up outside capture
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        fn_launch()
+    for _ in range(3):
+        g.replay()
+    stream.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e1.record(stream)
+    stream.synchronize()
+    del g
+    return e0.elapsed_time(e1) * 1e3 / (reps * calls_per_rep)
+
+
+def _q4_on_gpu(rows: int, cols: int, seed: int, dev):
+    import torch
+
+    from alveare_b200 import q4_quantize
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    w = torch.randn((rows, cols), generator=g, device=dev, dtype=torch.float32).mul_(0.02)
+    out = q4_quantize(w)
+    del w
+    return out
+
+
+def extra_configs(device: int) -> dict:
+    """BASELINE configs 1, 2 and 5 plus the decode-batch sweep, each through
+    the library's C ABI on weights rotated over more distinct copies than L2
+    holds (>= 4 x 126 MB), so every call streams its weights from HBM."""
+    import ctypes
+
+    import torch
+
+    from alveare_b200 import FusedFFNWeight, Q4Weight, _lib
+    dev = torch.device("cuda", device)
+    st = torch.cuda.Stream(device=dev)
+    sp = st.cuda_stream
+    ctx = _lib.context(device)
+    lib = ctx.lib
+    peak = load_peaks()["hbm_gbs"]
+    out = {}
+
+    # config 1: gemv 6912 x 1152, fp32 x and y, 128 weight copies (573 MB)
+    N1, K1, C1 = 6912, 1152, 128
+    ws = [Q4Weight(_q4_on_gpu(N1, K1, 10_000 + i, dev), N=N1, K=K1, device=device) for i in range(C1)]
+    x = torch.randn(K1, device=dev)
+    y = torch.empty(N1, device=dev)
+
+    def gemv_all():
+        for w in ws:
+            ctx.check(lib.alv_gemv(ctx.ptr, w.handle, 1, x.data_ptr(), _lib.F32, y.data_ptr(), _lib.F32, sp), "gemv")
+    us = _time_graph(gemv_all, 10, C1, st)
+    b1 = N1 * K1 // 32 * 18 + K1 * 4 + N1 * 4
+    out["config1_gemv_6912x1152"] = {"us_per_call": round(us, 3), "gbs": round(b1 / us / 1e3, 1),
+                                     "frac_of_hbm": round(b1 / us / 1e3 / peak, 4), "bytes_per_call": b1,
+                                     "rotation": f"{C1} weight copies, {C1 * N1 * K1 // 32 * 18 / 1e6:.0f} MB"}
+    for w in ws:
+        w.free()
+    del ws
+
+    # config 2: Gemma-3-1B FFN 1152 x 6912, GeGLU, fp32 x and y, 128 copies (1.72 GB)
+    H2, I2, C2 = 1152, 6912, 128
+    fs = []
+    for i in range(C2):
+        g_, u_, d_ = (_q4_on_gpu(r, c, 20_000 + 3 * i + m, dev) for m, (r, c) in enumerate(((I2, H2), (I2, H2), (H2, I2))))
+        fs.append(FusedFFNWeight(g_, u_, d_, H2, I2, "gelu", device=device))
+        del g_, u_, d_
+    x2 = torch.randn(H2, device=dev)
+    y2 = torch.empty(H2, device=dev)
+
+    def ffn_all():
+        for f in fs:
+            ctx.check(lib.alv_ffn(ctx.ptr, f.handle, 1, x2.data_ptr(), _lib.F32, y2.data_ptr(), _lib.F32, sp), "ffn")
+    us = _time_graph(ffn_all, 10, C2, st)
+    b2 = 3 * H2 * I2 // 32 * 18 + H2 * 8
+    out["config2_ffn_1152x6912_geglu"] = {"us_per_call": round(us, 3), "gbs": round(b2 / us / 1e3, 1),
+                                          "frac_of_hbm": round(b2 / us / 1e3 / peak, 4), "bytes_per_call": b2,
+                                          "rotation": f"{C2} FFN copies, {C2 * b2 / 1e9:.2f} GB"}
+    for f in fs:
+        f.free()
+    del fs
+
+    # config 5: prefill gemm 512 x 3840 x 15360 (tcgen05) and the decode-batch
+    # sweep on the same shape, 8 weight copies (265 MB)
+    N5, K5, B5, C5 = 15360, 3840, 512, 8
+    ws = [Q4Weight(_q4_on_gpu(N5, K5, 30_000 + i, dev), N=N5, K=K5, device=device) for i in range(C5)]
+    X = torch.randn((B5, K5), device=dev).to(torch.bfloat16)
+    Y = torch.empty((B5, N5), device=dev)
+
+    def gemm_all():
+        for w in ws:
+            ctx.check(lib.alv_gemm(ctx.ptr, w.handle, B5, X.data_ptr(), Y.data_ptr(), _lib.F32, sp), "gemm")
+    us = _time_graph(gemm_all, 10, C5, st)
+    flop = 2 * B5 * K5 * N5
+    out["config5_prefill_gemm_512x3840x15360"] = {
+        "us_per_call": round(us, 2), "tflops": round(flop / us / 1e6, 1),
+        "frac_of_bf16_peak": round(flop / us / 1e6 / load_peaks_tc(), 4), "flop_per_call": flop,
+        "rotation": f"{C5} weight copies, {C5 * N5 * K5 // 32 * 18 / 1e6:.0f} MB"}
+    sweep = {}
+    for B in (1, 2, 4, 8, 16):
+        xb = torch.randn((B, K5), device=dev).to(torch.bfloat16)
+        yb = torch.empty((B, N5), device=dev)
+
+        def gemv_b(xb=xb, yb=yb, B=B):
+            for w in ws:
+                ctx.check(lib.alv_gemv(ctx.ptr, w.handle, B, xb.data_ptr(), _lib.BF16, yb.data_ptr(), _lib.F32, sp),
+                          "gemv")
+        us = _time_graph(gemv_b, 20, C5, st)
+        bb = N5 * K5 // 32 * 18 + B * (K5 * 2 + N5 * 4)
+        sweep[str(B)] = {"us_per_call": round(us, 2), "gbs": round(bb / us / 1e3, 1),
+                         "frac_of_hbm": round(bb / us / 1e3 / peak, 4), "tokens_per_s": round(B / us * 1e6, 1)}
+    out["decode_batch_sweep_15360x3840"] = sweep
+    for w in ws:
+        w.free()
+    torch.cuda.synchronize(dev)
+    return out
+
+
+def load_peaks_tc() -> float:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return float(json.load(open(p))["bf16_tflops"])
+    return 1590.0
 
 # ---------------------------------------------------------------------------
 # our arm
@@ -351,6 +499,8 @@ def run_ours(args) -> None:
         "gpu_launches": step_launches * args.steps,
         "clocks": clock_info,
     }
+    if rank == 0 and world == 1 and not args.no_extras:
+        line["other_configs"] = extra_configs(local)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = {k: v for k, v in cpu_baseline().items() if k != "s_per_layer"}
     stack.release()
@@ -364,10 +514,11 @@ def run_ours(args) -> None:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true", help="skip the config 1/2/5 measurements")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="stack depth (default 48, the benchmark workload; smaller only for profiling captures)")
     args = ap.parse_args()

@@ -64,6 +64,13 @@ int alv_ctx_create(int device, alv_ctx** out);
 int alv_ctx_destroy(alv_ctx* ctx);
 const char* alv_last_error(const alv_ctx* ctx);
 
+/* info[0..7] = device, SM count, scratch-arena bytes, host-call staging
+ * bytes, device allocations the context has made so far (every cudaMalloc of
+ * the library on its behalf: sync block, arena growth, weights, staging),
+ * registered handles, 0, 0.  Diagnostics; no counterpart in the reference
+ * (its registry keeps per-shape buffer objects, npu.cpp:59-72). */
+int alv_ctx_info(alv_ctx* ctx, int64_t* info);
+
 /* Synchronize `stream` and report any device-side failure recorded since the
  * last call (ALV_ERR_TIMEOUT).  Clears the recorded status. */
 int alv_sync_status(alv_ctx* ctx, void* stream);
@@ -114,7 +121,9 @@ int alv_weight_dequantize(alv_ctx* ctx, alv_handle h, int which, uint16_t* out, 
 /* ---- compute (device pointers, stream-ordered) ---------------------------- */
 
 /* y[t, n] = sum_k W[n, k] * x[t, k] for t < ntok (1 <= ntok <= 16; fp32 x
- * allows ntok <= 8).  x is (ntok, K), y is (ntok, N), both row-major.
+ * allows ntok <= 8).  x is (ntok, K), y is (ntok, N), both row-major; x must
+ * be 8-byte (fp32) or 4-byte (bf16) aligned, else ALV_ERR_ARG (the kernels
+ * read x in element pairs).
  * Replaces NpuRegistry::run_gemv / run_gemm (npu.cpp:269-312) and the
  * gemv_q / gemm_q NPU kernels (kernels/gemv_q/gemv_q.cc:14-73,
  * kernels/gemm_q/gemm_q.cc:18-54). */
@@ -132,7 +141,7 @@ int alv_gemm(alv_ctx* ctx, alv_handle h, int B, const uint16_t* x, void* y, int 
 
 /* Fused FFN on the registered slice: gate = bf16(Wg x), up = bf16(Wu x),
  * act = bf16(act_fn(gate) * up), y = Wd act (fp32 accumulate).  x is
- * (ntok, H), y is (ntok, H); 1 <= ntok <= 8.  For a tensor-parallel slice y
+ * (ntok, H), y is (ntok, H); 1 <= ntok <= 8; x aligned as for alv_gemv.  For a tensor-parallel slice y
  * is this device's partial sum (use ALV_F32 and all-reduce).  Replaces
  * NpuRegistry::run_ffn_fused (npu.cpp:340-378) including its host partial
  * sum, and the ffn_fused NPU design (kernels/ffn_fused/ffn_fused.py:28-328). */
@@ -200,18 +209,29 @@ int alv_activation(alv_ctx* ctx, int act, int n, const uint16_t* gate, const uin
 int alv_ffn_stack_exchange(alv_ctx* ctx, alv_handle stack, int world, void* blob);
 int alv_ffn_stack_connect(alv_ctx* ctx, alv_handle stack, int rank, int world, const void* blobs);
 
+/* Test probe: when `down_last` is a device buffer of (ntok, H) fp32, every
+ * later alv_ffn_stack_run of this stack also writes the last layer's down
+ * projection there, exactly as the final residual step read it (summed over
+ * the split-K partials and, for a tensor-parallel stack, over the ranks in
+ * rank order), so a layer can be checked against the CPU path before the
+ * bf16 rounding of the residual stream.  NULL turns it off.  No counterpart
+ * in the reference (its host sum, npu.cpp:360-377, is visible to the caller). */
+int alv_ffn_stack_set_probe(alv_ctx* ctx, alv_handle stack, float* down_last);
+
 /* Allocation-free gemv: same arithmetic and arguments as alv_gemv, for
  * callers that must not allocate device memory while they run (a decode
  * loop with a fixed GPU memory budget, a host runtime that owns the device
  * allocator, code that cannot afford the device synchronization of
  * cudaMalloc/cudaFree).  alv_gemv may grow the context's scratch arena on
  * the first larger call; this entry point never allocates: its split-K
- * workspace and counters live in a static device array of 1,277,952 bytes
+ * workspace and counters live in a static device array of 141,312 bytes
  * that every GPU loading the library holds until process exit.  Limits:
- * ntok <= 4, N <= 262,144 rows, GPUs with <= 148 SMs; larger requests return
- * ALV_ERR_UNSUPPORTED.  The first call on a device looks up the array's
- * device address (cudaGetSymbolAddress), so make that first call before any
- * stream capture.  All calls share the one array: calls that overlap on the
+ * ntok <= 4, N <= 262,144 rows, GPUs with <= 148 SMs (one CTA per SM);
+ * larger requests return ALV_ERR_UNSUPPORTED.  The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress) and keeps it
+ * for the life of the process, so make that first call before any stream
+ * capture, and do not call cudaDeviceReset on a device this entry point has
+ * used (the kept address would then be stale).  All calls share the one array: calls that overlap on the
  * GPU (different streams, or concurrent host threads) race and must be
  * serialized by the caller.  No counterpart in the reference. */
 int alv_gemv_noalloc(alv_ctx* ctx, alv_handle h, int ntok, const void* x, int x_dtype, void* y,

@@ -1,9 +1,9 @@
 """Generate the committed golden fixtures by running the REFERENCE's own code.
 
-Run in a container where the reference project is available (read-only) at
-``$ALVEARE_REFERENCE`` (default ``/root/reference``):
+Run where a checkout of the reference project is available (read-only) and
+name its root in ``ALVEARE_REFERENCE``:
 
-    python tests/golden/make_golden.py
+    ALVEARE_REFERENCE=/path/to/alveare python tests/golden/make_golden.py
 
 It imports the reference's ``tools/convert/gemv_q_convert.py``
 (``quantize_to_q4_0``, ``pack_to_combined``) and ``tools/ref/gemv_q.py``
@@ -30,12 +30,18 @@ from pathlib import Path
 import numpy as np
 from ml_dtypes import bfloat16
 
-REF = Path(os.environ.get("ALVEARE_REFERENCE", "/root/reference"))
 OUT = Path(__file__).resolve().parent
 
 
+def _reference_root() -> Path:
+    root = os.environ.get("ALVEARE_REFERENCE")
+    if not root:
+        raise SystemExit("set ALVEARE_REFERENCE to the root of a checkout of the reference project")
+    return Path(root)
+
+
 def _ref():
-    sys.path.insert(0, str(REF))
+    sys.path.insert(0, str(_reference_root()))
     from tools.convert.gemv_q_convert import pack_to_combined, quantize_to_q4_0
     from tools.ref.gemv_q import dequantize_combined, gemv_q_combined
     return quantize_to_q4_0, pack_to_combined, dequantize_combined, gemv_q_combined

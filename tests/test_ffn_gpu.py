@@ -163,3 +163,19 @@ def test_ffn_generic_dequant_path_shared_by_both_matrices():
     info = fw.info()
     assert info[3] == 0 and info[4] == 0
     assert normwise(run_ffn(fw, x)[0], ref) <= TOL
+
+
+def test_ffn_fused_npu_batch_of_tokens():
+    """ffn_fused_npu with a (B, H) batch: y of every token lands in row 0 of
+    Y_partial (n_rows, B, H), the other rows are zeroed."""
+    H, I, B = 512, 1024, 4
+    cg, cu, cd, _ = make_ffn(H, I, 77)
+    X = np.random.default_rng(78).normal(0, 1, (B, H)).astype(np.float32)
+    ref, _, _, _ = q4.ffn(cg, cu, cd, X, "gelu")
+    fw = pack_ffn_fused_weights(cg, cu, cd, H, I)
+    Yp = torch.full((2, B, H), 7.0, dtype=torch.float32, device="cuda")
+    ffn_fused_npu(fw, torch.from_numpy(X).cuda(), Yp, H=H, I=I, activation="gelu")
+    fw.ctx.sync_status()
+    assert normwise(Yp.sum(0).cpu().numpy(), ref) <= TOL
+    assert torch.count_nonzero(Yp[1]) == 0
+    fw.free()

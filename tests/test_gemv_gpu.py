@@ -13,7 +13,7 @@ import pytest
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
-from alveare_b200 import Q4Weight, gemm_q_npu, gemv_q_npu, q4_quantize  # noqa: E402
+from alveare_b200 import Q4Weight, _lib, gemm_q_npu, gemv_q_npu, q4_quantize  # noqa: E402
 from oracle import q4  # noqa: E402
 
 TOL = 1e-3
@@ -215,3 +215,59 @@ def test_gemv_zero_matrix_and_zero_x():
     w = Q4Weight(comb)
     y = run_gemv(w, np.ones(K, np.float32))
     assert np.all(y == 0)
+
+
+@pytest.mark.parametrize("xdt,off", [(torch.float32, 4), (torch.bfloat16, 2)])
+def test_gemv_and_ffn_reject_misaligned_x_without_launching(xdt, off):
+    """An activation view at an odd element offset (x[1:] of a buffer) is
+    refused with ALV_ERR_ARG before any kernel is launched: the kernels read
+    x in element pairs (8-byte fp32 / 4-byte bf16 loads)."""
+    from alveare_b200 import FusedFFNWeight
+    rng = np.random.default_rng(3)
+    K, N = 256, 64
+    w = Q4Weight(q4.quantize_combined(rng.normal(0, 0.02, (N, K)).astype(np.float32)))
+    buf = torch.zeros(K + 8, dtype=xdt, device="cuda")
+    y = torch.empty(N, dtype=torch.float32, device="cuda")
+    code = _lib.F32 if xdt == torch.float32 else _lib.BF16
+    st = torch.cuda.current_stream().cuda_stream
+    ctx = w.ctx
+    assert ctx.lib.alv_gemv(ctx.ptr, w.handle, 1, buf.data_ptr() + off, code, y.data_ptr(), _lib.F32, st) == 1
+    assert b"aligned" in ctx.lib.alv_last_error(ctx.ptr)
+    assert ctx.lib.alv_gemv_noalloc(ctx.ptr, w.handle, 1, buf.data_ptr() + off, code, y.data_ptr(), _lib.F32,
+                                    st) == 1
+    H, I = 256, 512
+    f = FusedFFNWeight(*(q4.quantize_combined(rng.normal(0, 0.02, s).astype(np.float32))
+                         for s in ((I, H), (I, H), (H, I))), H, I, "gelu")
+    yf = torch.empty(H, dtype=torch.float32, device="cuda")
+    assert ctx.lib.alv_ffn(ctx.ptr, f.handle, 1, buf.data_ptr() + off, code, yf.data_ptr(), _lib.F32, st) == 1
+    ctx.sync_status()
+    w.free()
+    f.free()
+
+
+def test_raw_buffer_is_repacked_once():
+    """gemv_q_npu / gemm_q_npu given the reference's raw packed buffer repack
+    it on the first call only: the second call with the same buffer reuses the
+    resident copy (no new weight handle, no device allocation)."""
+    from alveare_b200 import ops
+    ops.clear_weight_cache()
+    rng = np.random.default_rng(12)
+    N, K = 512, 1024
+    comb = torch.from_numpy(q4.quantize_combined(rng.normal(0, 0.02, (N, K)).astype(np.float32))).cuda()
+    x = torch.from_numpy(rng.normal(0, 1, K).astype(np.float32)).cuda()
+    y1 = torch.empty(N, device="cuda")
+    y2 = torch.empty(N, device="cuda")
+    ctx = _lib.context(0)
+    gemv_q_npu(comb, x, y1, N=N, K=K)
+    before = ctx.info()
+    gemv_q_npu(comb, x, y2, N=N, K=K)
+    X = x.reshape(1, K).repeat(3, 1)
+    Y = torch.empty((3, N), device="cuda")
+    gemm_q_npu(comb, X, Y, B=3, N=N, K=K)
+    after = ctx.info()
+    assert after["handles"] == before["handles"] and after["allocs"] == before["allocs"]
+    assert torch.equal(y1, y2) and torch.equal(Y[1], y1)
+    comb.add_(0)   # an in-place torch change bumps the version: repacked again
+    gemv_q_npu(comb, x, y2, N=N, K=K)
+    assert ctx.info()["handles"] == after["handles"] + 1
+    ops.clear_weight_cache()
