@@ -64,6 +64,14 @@ SIGNATURES = {
     "alv_set_trace": (_i, [_vp, _vp]),
     "alv_ctx_info": (_i, [_vp, _c.POINTER(_c.c_int64)]),
     "alv_ffn_stack_set_probe": (_i, [_vp, _u32, _vp]),
+    "alv_llama_create": (_i, [_vp, _vp, _c.POINTER(_u32)]),
+    "alv_llama_load": (_i, [_vp, _u32, _c.c_char_p, _vp, _sz, _i]),
+    "alv_llama_start": (_i, [_vp, _u32, _vp, _i, _vp]),
+    "alv_llama_run": (_i, [_vp, _u32, _i, _i, _vp]),
+    "alv_llama_tokens": (_i, [_vp, _u32, _i, _i, _vp, _vp]),
+    "alv_llama_generate": (_i, [_vp, _u32, _vp, _i, _i, _vp, _vp]),
+    "alv_llama_forward": (_i, [_vp, _u32, _i, _i, _vp, _vp]),
+    "alv_llama_reset": (_i, [_vp, _u32, _vp]),
 }
 
 _lock = threading.Lock()

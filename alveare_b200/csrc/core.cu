@@ -3,8 +3,7 @@
 // load-time repack (reference 20-byte blocks -> unit layout), dequantize,
 // the activation op, the stack finalize step and the host-buffer calls.
 // Kernel families live in gemv.cu, ffn.cu, stack.cu, gemm.cu and decode.cu.
-#include "internal.h"
-#include "kernels.cuh"
+#include "launch.h"
 #include "loadtime.cuh"
 
 namespace alv {
@@ -62,10 +61,10 @@ int check_status(alv_ctx* ctx, cudaStream_t st) {
   // launch's status, barrier and counters.
   if (s) ALV_CUDA(ctx, cudaMemset(ctx->sync, 0, kSyncBytes));
   for (auto& w : ctx->weights) {
-    if (!w || w->kind != 3) continue;
+    if (!w || (w->kind != 3 && w->kind != 4) || !w->ws) continue;
     uint32_t t = 0;
     ALV_CUDA(ctx, cudaMemcpy(&t, w->ws, sizeof(t), cudaMemcpyDeviceToHost));
-    if (t) ALV_CUDA(ctx, cudaMemset(w->ws, 0, stack_sync_bytes(w.get())));
+    if (t) ALV_CUDA(ctx, cudaMemset(w->ws, 0, w->kind == 3 ? stack_sync_bytes(w.get()) : w->sync_bytes));
     // The peer-barrier counters of a tensor-parallel stack are out of step
     // across ranks after a wait gave up: only re-creating it on every rank
     // restores them.
@@ -188,6 +187,63 @@ int stage_source(alv_ctx* ctx, const void* src, size_t bytes, int on_device, con
 }
 
 }  // namespace
+
+int repack_rows(alv_ctx* ctx, const uint8_t* src, uint32_t rows, uint32_t K, Mat* out) {
+  RepackSrc s{};
+  s.a = src;
+  s.b = nullptr;
+  s.rows = rows;
+  s.row_off = 0;
+  s.row_bytes = static_cast<uint64_t>(K / 32) * 20;
+  s.blk_off = 0;
+  s.K = K;
+  s.interleave8 = 0;
+  s.RT = (rows + 15) / 16;
+  s.KT = (K + 63) / 64;
+  return build_mat(ctx, s, rows, K, out);
+}
+
+int repack_ffn(alv_ctx* ctx, const uint8_t* g, const uint8_t* u, const uint8_t* d, uint32_t H, uint32_t I,
+               uint32_t i_begin, uint32_t i_end, Mat* gu, Mat* dn) {
+  const uint32_t Il = i_end - i_begin;
+  RepackSrc sa{};
+  sa.a = g;
+  sa.b = u;
+  sa.rows = Il;
+  sa.row_off = i_begin;
+  sa.row_bytes = static_cast<uint64_t>(H / 32) * 20;
+  sa.blk_off = 0;
+  sa.K = H;
+  sa.interleave8 = 1;
+  sa.RT = (Il + 7) / 8;
+  sa.KT = (H + 63) / 64;
+  RepackSrc sb{};
+  sb.a = d;
+  sb.b = nullptr;
+  sb.rows = H;
+  sb.row_off = 0;
+  sb.row_bytes = static_cast<uint64_t>(I / 32) * 20;
+  sb.blk_off = i_begin / 32;
+  sb.K = Il;
+  sb.interleave8 = 0;
+  sb.RT = (H + 15) / 16;
+  sb.KT = (Il + 63) / 64;
+  // One kernel dequantizes both matrices: they share the dequant path.
+  Survey sva, svb;
+  int rc;
+  if (!(rc = survey_mat(ctx, sa, &sva)) && !(rc = survey_mat(ctx, sb, &svb))) {
+    if (!(sva.fast && svb.fast)) sva = svb = Survey{};
+    rc = repack_mat(ctx, sa, sva, Il, H, gu);
+    if (!rc) rc = repack_mat(ctx, sb, svb, H, Il, dn);
+  }
+  if (rc) {
+    cudaFree(gu->dev);
+    cudaFree(dn->dev);
+    gu->dev = dn->dev = nullptr;
+  }
+  return rc;
+}
+
 }  // namespace alv
 
 using namespace alv;
@@ -327,7 +383,6 @@ int alv_ffn_weight_create(alv_ctx* ctx, int H, int I, int act, const void* gate,
     cudaFree(od);
     return rc;
   }
-  const uint32_t Il = static_cast<uint32_t>(i_end - i_begin);
   auto w = std::make_unique<Weight>();
   w->kind = 2;
   w->H = static_cast<uint32_t>(H);
@@ -335,43 +390,11 @@ int alv_ffn_weight_create(alv_ctx* ctx, int H, int I, int act, const void* gate,
   w->i_begin = static_cast<uint32_t>(i_begin);
   w->i_end = static_cast<uint32_t>(i_end);
   w->act = act;
-  RepackSrc sa{};
-  sa.a = g;
-  sa.b = u;
-  sa.rows = Il;
-  sa.row_off = static_cast<uint32_t>(i_begin);
-  sa.row_bytes = static_cast<uint64_t>(H / 32) * 20;
-  sa.blk_off = 0;
-  sa.K = static_cast<uint32_t>(H);
-  sa.interleave8 = 1;
-  sa.RT = (Il + 7) / 8;
-  sa.KT = static_cast<uint32_t>((H + 63) / 64);
-  RepackSrc sb{};
-  sb.a = d;
-  sb.b = nullptr;
-  sb.rows = static_cast<uint32_t>(H);
-  sb.row_off = 0;
-  sb.row_bytes = static_cast<uint64_t>(I / 32) * 20;
-  sb.blk_off = static_cast<uint32_t>(i_begin / 32);
-  sb.K = Il;
-  sb.interleave8 = 0;
-  sb.RT = static_cast<uint32_t>((H + 15) / 16);
-  sb.KT = (Il + 63) / 64;
-  // One kernel dequantizes both matrices: they share the dequant path.
-  Survey sva, svb;
-  if (!(rc = survey_mat(ctx, sa, &sva)) && !(rc = survey_mat(ctx, sb, &svb))) {
-    if (!(sva.fast && svb.fast)) sva = svb = Survey{};
-    rc = repack_mat(ctx, sa, sva, Il, static_cast<uint32_t>(H), &w->a);
-    if (!rc) rc = repack_mat(ctx, sb, svb, static_cast<uint32_t>(H), Il, &w->b);
-  }
+  rc = repack_ffn(ctx, g, u, d, w->H, w->I, w->i_begin, w->i_end, &w->a, &w->b);
   cudaFree(og);
   cudaFree(ou);
   cudaFree(od);
-  if (rc) {
-    cudaFree(w->a.dev);
-    cudaFree(w->b.dev);
-    return rc;
-  }
+  if (rc) return rc;
   ctx->weights.push_back(std::move(w));
   *out = static_cast<alv_handle>(ctx->weights.size());
   return ALV_OK;

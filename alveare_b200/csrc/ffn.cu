@@ -1,7 +1,6 @@
 // Host side of the C ABI, part 3: the fused FFN (ffn_kernel), plain and with
 // the decode layer's norm/residual glue fused in.
-#include "internal.h"
-#include "kernels.cuh"
+#include "launch.h"
 
 namespace alv {
 namespace {
@@ -46,12 +45,13 @@ int launch_ffn_f(alv_ctx* ctx, const FfnParams& p, bool split, uint32_t nt, cuda
   return fail(ctx, ALV_ERR_UNSUPPORTED, "unsupported token count");
 }
 
-// Both FFN matrices were repacked for the same dequant path.
-int launch_ffn(alv_ctx* ctx, const FfnParams& p, bool split, uint32_t nt, cudaStream_t st) {
-  return p.gu.fast ? launch_ffn_f<true>(ctx, p, split, nt, st) : launch_ffn_f<false>(ctx, p, split, nt, st);
-}
 
 }  // namespace
+
+// Both FFN matrices were repacked for the same dequant path.
+int launch_ffn_params(alv_ctx* ctx, const FfnParams& p, bool split, uint32_t nt, cudaStream_t st) {
+  return p.gu.fast ? launch_ffn_f<true>(ctx, p, split, nt, st) : launch_ffn_f<false>(ctx, p, split, nt, st);
+}
 
 int do_ffn(alv_ctx* ctx, Weight* w, int ntok, const FfnIo& io, cudaStream_t st) {
   if (ntok < 1 || ntok > 8) return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn: ntok must be 1..8");
@@ -90,7 +90,7 @@ int do_ffn(alv_ctx* ctx, Weight* w, int ntok, const FfnIo& io, cudaStream_t st) 
   p.trace = ctx->trace;
   auto aligned16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
   p.glue_tma = io.glue && aligned16(io.x_in) && (!io.down_in || aligned16(io.down_in));
-  return launch_ffn(ctx, p, split, nt, st);
+  return launch_ffn_params(ctx, p, split, nt, st);
 }
 
 }  // namespace alv

@@ -1,7 +1,6 @@
 // Host side of the C ABI, part 2: the Q4 gemv (decode and decode-batch,
 // gemv_kernel) and its allocation-free variant.
-#include "internal.h"
-#include "kernels.cuh"
+#include "launch.h"
 
 namespace alv {
 namespace {
@@ -43,9 +42,6 @@ int launch_gemv_f(alv_ctx* ctx, const GemvParams& p, bool split, uint32_t ncols,
   return fail(ctx, ALV_ERR_UNSUPPORTED, "unsupported column count");
 }
 
-int launch_gemv(alv_ctx* ctx, const GemvParams& p, bool split, uint32_t ncols, cudaStream_t st) {
-  return p.m.fast ? launch_gemv_f<true>(ctx, p, split, ncols, st) : launch_gemv_f<false>(ctx, p, split, ncols, st);
-}
 
 // Shape and argument checks shared by alv_gemv and alv_gemv_noalloc.
 int gemv_args(alv_ctx* ctx, int ntok, const void* x, int x_dtype, const char* who, uint32_t* ncols) {
@@ -70,6 +66,10 @@ GemvParams gemv_params(Weight* w, int ntok, const void* x, int x_dtype, void* y,
 
 }  // namespace
 
+int launch_gemv_params(alv_ctx* ctx, const GemvParams& p, bool split, uint32_t ncols, cudaStream_t st) {
+  return p.m.fast ? launch_gemv_f<true>(ctx, p, split, ncols, st) : launch_gemv_f<false>(ctx, p, split, ncols, st);
+}
+
 int do_gemv(alv_ctx* ctx, Weight* w, int ntok, const void* x, int x_dtype, void* y, int y_dtype,
             cudaStream_t st) {
   uint32_t ncols = 0;
@@ -82,7 +82,7 @@ int do_gemv(alv_ctx* ctx, Weight* w, int ntok, const void* x, int x_dtype, void*
   GemvParams p = gemv_params(w, ntok, x, x_dtype, y, y_dtype);
   p.fx = Fixup{reinterpret_cast<float*>(work_ptr(ctx)), counters_ptr(ctx)};
   p.status = status_ptr(ctx);
-  return launch_gemv(ctx, p, x_dtype == ALV_F32, ncols, st);
+  return launch_gemv_params(ctx, p, x_dtype == ALV_F32, ncols, st);
 }
 
 }  // namespace alv
@@ -176,5 +176,5 @@ extern "C" int alv_gemv_noalloc(alv_ctx* ctx, alv_handle h, int ntok, const void
   GemvParams p = gemv_params(w, ntok, x, x_dtype, y, y_dtype);
   p.fx = Fixup{reinterpret_cast<float*>(base + kNoAllocCounterBytes), reinterpret_cast<uint32_t*>(base)};
   p.status = status_ptr(ctx);
-  return launch_gemv(ctx, p, x_dtype == ALV_F32, ncols, st);
+  return launch_gemv_params(ctx, p, x_dtype == ALV_F32, ncols, st);
 }

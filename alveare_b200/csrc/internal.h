@@ -43,14 +43,15 @@ struct Weight {
   // stack's own workspace (sync words, split-K partials, down, act)
   std::vector<alv_handle> layers;
   struct LayerW* layers_dev = nullptr;
-  uint8_t* ws = nullptr;
+  uint8_t* ws = nullptr;     // kinds 3, 4: workspace, starting with the sync block
   size_t ws_bytes = 0;
+  size_t sync_bytes = 0;     // kind 4: bytes of the sync block (status, grid barrier, counters)
   // kind 3, tensor parallel: this rank's exchange region (cudaMalloc, shared
   // with the peers by CUDA IPC) and every rank's region as mapped here
   int world = 1, rank = 0;
   bool connected = false, broken = false;
   uint8_t* xlocal = nullptr;
-  uint32_t xslot = 0, xws_off = 0;
+  uint32_t xslot = 0, xws_off = 0;  // exchange slot: LL words per slot, offset of the CTA partials
   uint8_t* xr[kMaxRanksHost] = {};
   unsigned char blob[ALV_IPC_BLOB_BYTES] = {};
   float* probe = nullptr;  // kind 3: optional fp32 copy of the last layer's down projection

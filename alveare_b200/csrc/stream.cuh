@@ -79,22 +79,24 @@ __host__ __device__ __forceinline__ uint32_t warp_of_unit(uint64_t u, uint64_t U
 
 // How a matrix's RT x KT units are split over the grid: CTA c owns one
 // contiguous unit range and its warps split that range.  Row-aligned when
-// every CTA can take whole row tiles at < 1/32 imbalance (then no row tile
-// spans two CTAs and the split-K reduction stays in shared memory);
-// otherwise unit-balanced: W participating warps numbered CTA-major, warp gw
-// owning [gw*U/W, (gw+1)*U/W).
+// asked for (`row_aligned`: the FFN's gate/up matrices, whose split-K
+// reduction then never leaves the CTA) or when every CTA can take whole row
+// tiles at < 1/32 imbalance (then no row tile spans two CTAs and the split-K
+// reduction stays in shared memory); otherwise unit-balanced: W
+// participating warps numbered CTA-major, warp gw owning [gw*U/W, (gw+1)*U/W).
+// A row-aligned split of RT < nctas row tiles leaves CTAs without work.
 struct Partition {
   uint64_t U, W;
   uint32_t RT, KT, nctas, aligned;
 
-  __host__ __device__ static Partition make(uint32_t RT, uint32_t KT, uint32_t nctas) {
+  __host__ __device__ static Partition make(uint32_t RT, uint32_t KT, uint32_t nctas, bool row_aligned = false) {
     Partition p;
     p.RT = RT;
     p.KT = KT;
     p.nctas = nctas;
     p.U = static_cast<uint64_t>(RT) * KT;
     const uint64_t per = (static_cast<uint64_t>(RT) + nctas - 1) / nctas;
-    p.aligned = RT >= nctas && per * nctas * 32 <= static_cast<uint64_t>(RT) * 33;
+    p.aligned = row_aligned || (RT >= nctas && per * nctas * 32 <= static_cast<uint64_t>(RT) * 33);
     p.W = effective_warps(static_cast<uint64_t>(nctas) * kWarpsPerCtaS, p.U, KT);
     return p;
   }
@@ -611,9 +613,9 @@ __device__ __forceinline__ void flush_tile(const float (&acc)[(NCOLS > 8 ? 2 : 1
 // ones inside the CTA's range.  Row tiles shared with other CTAs (unit-
 // balanced partitions only) get a CTA partial in fx.ws; unless DEFER, the
 // last CTA to arrive (acq_rel counter) sums them in CTA order and applies
-// epi.  With DEFER the partials are left for the consumer of the result to
-// sum after the next grid barrier (SplitRows).  All warps of the CTA call
-// this (it syncs them).
+// epi.  With DEFER the partials go to epi.park(cta, slot, element, value)
+// and the consumer of the result sums them (the FFN stack's next glue).
+// All warps of the CTA call this (it syncs them).
 // ---------------------------------------------------------------------------
 template <bool DEFER = false, class Epi>
 __device__ void cta_fixup(const Partition& pt, const uint32_t* wr, const Fixup& fx, int ntok, const Epi& epi) {
@@ -654,9 +656,9 @@ __device__ void cta_fixup(const Partition& pt, const uint32_t* wr, const Fixup& 
       }
       if (inside) {
         epi.apply(r, g, tok, vg, vg8);
-      } else if constexpr (DEFER) {  // the epilogue may pre-scale parked partials
-        cpart[tok * 16 + g] = epi.park(vg);
-        cpart[tok * 16 + g + 8] = epi.park(vg8);
+      } else if constexpr (DEFER) {  // the epilogue stores (and may pre-scale) parked partials
+        epi.park(c, cslot, tok * 16 + g, vg);
+        epi.park(c, cslot, tok * 16 + g + 8, vg8);
       } else {
         cpart[tok * 16 + g] = vg;
         cpart[tok * 16 + g + 8] = vg8;

@@ -218,6 +218,65 @@ int alv_ffn_stack_connect(alv_ctx* ctx, alv_handle stack, int rank, int world, c
  * in the reference (its host sum, npu.cpp:360-377, is visible to the caller). */
 int alv_ffn_stack_set_probe(alv_ctx* ctx, alv_handle stack, float* down_last);
 
+/* ---- Llama greedy decode on the GPU --------------------------------------
+ * The reference's Llama decode step (runtime/py/model.py:821-934 with its
+ * NPU matmuls, runtime/cpp/src/model.cpp:297-404 and the greedy loop of
+ * runtime/cpp/src/generator.cpp:15-52) with every stage on the device: Q4
+ * QKV / O / FFN / LM-head matmuls, RMSNorm, RoPE, a bf16 KV cache, GQA
+ * attention, residuals and the argmax.  Rounding points follow the
+ * reference's CPU path (bf16 after every projection, norm and residual).  A
+ * step reads its position and token from device memory, so the library
+ * captures it once into a CUDA graph and replays it per token. */
+typedef struct {
+  int32_t hidden, intermediate, heads, kv_heads, head_dim, layers, vocab, max_seq;
+  float rms_eps;        /* 1e-5 for Llama (model.py:532) */
+  int32_t reserved[7];
+} alv_llama_config;
+
+int alv_llama_create(alv_ctx* ctx, const alv_llama_config* cfg, alv_handle* out);
+
+/* Load one tensor by its name in the reference's quantized-model directory
+ * (tools/quantize_model.py:39-125, read by runtime/py/model.py:38-127):
+ *   "token_embd"                    float16 (vocab, hidden)
+ *   "output_norm.weight", "blk.{l}.attn_norm.weight", "blk.{l}.ffn_norm.weight"
+ *                                   float32 (hidden)
+ *   "blk.{l}.{attn_q,attn_k,attn_v,attn_output,ffn_gate,ffn_up,ffn_down}.weight_packed",
+ *   "lm_head_packed"                Q4 (rows, cols/32*20) uint8; K, V and the
+ *                                   LM head may carry zero padding rows
+ *   "rope_table"                    bf16 (max_seq, 2*head_dim): cos | sin per
+ *                                   position (model.py:230-261)
+ * `data` is host memory (on_device = 0) or device memory (1). */
+int alv_llama_load(alv_ctx* ctx, alv_handle model, const char* name, const void* data, size_t nbytes,
+                   int on_device);
+
+/* Start a sequence: zero the KV cache, put the prompt (host int32 ids) at
+ * positions 0..n_prompt-1 and the position at 0.  The first call on a model
+ * repacks its weights and captures the step graphs. */
+int alv_llama_start(alv_ctx* ctx, alv_handle model, const int32_t* prompt, int n_prompt, void* stream);
+
+/* Enqueue n_prompt_steps steps without logits (prompt tokens), then
+ * n_decode_steps greedy steps (LM head + argmax, the token written to the
+ * next position).  Asynchronous, stream-ordered. */
+int alv_llama_run(alv_ctx* ctx, alv_handle model, int n_prompt_steps, int n_decode_steps, void* stream);
+
+/* Copy token ids [first, first + n) of the sequence to host memory
+ * (synchronizes `stream`, reports device-side failures). */
+int alv_llama_tokens(alv_ctx* ctx, alv_handle model, int first, int n, int32_t* out_host, void* stream);
+
+/* start + run(n_prompt - 1, steps) + tokens(n_prompt, steps): the greedy loop
+ * of tests/test_generation.py:72-99 without an EOS stop.  n_prompt + steps
+ * must not exceed max_seq. */
+int alv_llama_generate(alv_ctx* ctx, alv_handle model, const int32_t* prompt, int n_prompt, int steps,
+                       int32_t* out_host, void* stream);
+
+/* One step at an explicit position, outside any graph: token -> KV cache at
+ * `pos`; with `logits` (device, vocab bf16) also the LM head output
+ * (model.py:919-934 forward(token, pos)). */
+int alv_llama_forward(alv_ctx* ctx, alv_handle model, int token, int pos, uint16_t* logits, void* stream);
+
+/* Zero the KV cache and the position (runtime/py/model.py reset_caches). */
+int alv_llama_reset(alv_ctx* ctx, alv_handle model, void* stream);
+
 /* Allocation-free gemv: same arithmetic and arguments as alv_gemv, for
  * callers that must not allocate device memory while they run (a decode
  * loop with a fixed GPU memory budget, a host runtime that owns the device
