@@ -69,6 +69,7 @@ SIGNATURES = {
     "alv_llama_start": (_i, [_vp, _u32, _vp, _i, _vp]),
     "alv_llama_run": (_i, [_vp, _u32, _i, _i, _vp]),
     "alv_llama_tokens": (_i, [_vp, _u32, _i, _i, _vp, _vp]),
+    "alv_llama_predicted": (_i, [_vp, _u32, _i, _i, _vp, _vp]),
     "alv_llama_generate": (_i, [_vp, _u32, _vp, _i, _i, _vp, _vp]),
     "alv_llama_forward": (_i, [_vp, _u32, _i, _i, _vp, _vp]),
     "alv_llama_reset": (_i, [_vp, _u32, _vp]),

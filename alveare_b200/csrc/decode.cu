@@ -34,7 +34,8 @@ struct LlamaModel {
   uint16_t *x = nullptr, *xn = nullptr, *qkvb = nullptr, *q = nullptr, *attn = nullptr, *proj = nullptr,
            *logits = nullptr;
   DecodeState* state = nullptr;
-  int* tokens = nullptr;       // [max_seq + 1]
+  int* tokens = nullptr;       // [max_seq + 1] token at each position
+  int* pred = nullptr;         // [max_seq + 1] the argmax each logits step predicted for the next position
   // workspace (Weight::ws): [sync block: status, grid barrier, counters][split-K partials][FFN act]
   uint32_t* status = nullptr;
   GridBar* bar = nullptr;
@@ -166,7 +167,7 @@ int gemv_into(alv_ctx* ctx, LlamaModel* m, const Mat& mat, const uint16_t* x, ui
   p.epi = RowsEpi{nullptr, y, mat.rows, mat.rows, mat.m.scale_mul};
   p.fx = Fixup{m->ws_gemv, m->cnt};
   p.status = m->status;
-  return launch_gemv_params(ctx, p, false, 1, st);
+  return launch_gemv_params(ctx, p, false, 1, st, true);
 }
 
 int ffn_into(alv_ctx* ctx, LlamaModel* m, int l, const uint16_t* x, uint16_t* y, cudaStream_t st) {
@@ -193,31 +194,36 @@ int enqueue_step(alv_ctx* ctx, LlamaModel* m, bool logits, cudaStream_t st) {
   const alv_llama_config& c = m->cfg;
   const int H = c.hidden, L = c.layers;
   const float eps = c.rms_eps;
-  embed_norm_kernel<<<1, kDecodeThreads, 0, st>>>(m->emb, m->state, m->tokens, H, m->norms, eps, m->x, m->xn);
-  ALV_CUDA(ctx, cudaGetLastError());
+  int rc = launch_ex(ctx, embed_norm_kernel, dim3(1), dim3(kDecodeThreads), 0, st, true,
+                     static_cast<const uint16_t*>(m->emb), static_cast<const DecodeState*>(m->state),
+                     static_cast<const int*>(m->tokens), H, static_cast<const float*>(m->norms), eps, m->x, m->xn);
+  if (rc) return rc;
   const size_t kv_layer = static_cast<size_t>(c.kv_heads) * c.max_seq * c.head_dim;
   const size_t attn_smem = static_cast<size_t>(c.head_dim + c.max_seq + kAttnThreads) * sizeof(float);
-  int rc;
   for (int l = 0; l < L; ++l) {
     if ((rc = gemv_into(ctx, m, m->qkv[l], m->xn, m->qkvb, st))) return rc;
     const RopeParams rp{m->qkvb, m->rope, m->state, m->kcache + l * kv_layer, m->vcache + l * kv_layer, m->q,
                         c.heads, c.kv_heads, c.head_dim, c.max_seq};
-    rope_cache_kernel<<<1, kDecodeThreads, 0, st>>>(rp);
-    ALV_CUDA(ctx, cudaGetLastError());
+    if ((rc = launch_ex(ctx, rope_cache_kernel, dim3(1), dim3(kDecodeThreads), 0, st, true, rp))) return rc;
     const AttnParams ap{m->q, m->kcache + l * kv_layer, m->vcache + l * kv_layer, m->state, m->attn,
                         c.heads, c.kv_heads, c.head_dim, c.max_seq, 1.0 / std::sqrt(static_cast<double>(c.head_dim))};
-    attention_kernel<<<c.heads, kAttnThreads, attn_smem, st>>>(ap);
-    ALV_CUDA(ctx, cudaGetLastError());
+    if ((rc = launch_ex(ctx, attention_kernel, dim3(c.heads), dim3(kAttnThreads), attn_smem, st, true, ap))) return rc;
     if ((rc = gemv_into(ctx, m, m->o[l], m->attn, m->proj, st))) return rc;
-    residual_norm_kernel<<<1, kDecodeThreads, 0, st>>>(m->x, m->proj, H, m->norms + (2 * l + 1) * H, eps, m->xn);
-    ALV_CUDA(ctx, cudaGetLastError());
+    if ((rc = launch_ex(ctx, residual_norm_kernel, dim3(1), dim3(kDecodeThreads), 0, st, true, m->x,
+                        static_cast<const uint16_t*>(m->proj), H, static_cast<const float*>(m->norms + (2 * l + 1) * H),
+                        eps, m->xn)))
+      return rc;
     if ((rc = ffn_into(ctx, m, l, m->xn, m->proj, st))) return rc;
-    residual_norm_kernel<<<1, kDecodeThreads, 0, st>>>(m->x, m->proj, H, m->norms + (2 * l + 2) * H, eps, m->xn);
-    ALV_CUDA(ctx, cudaGetLastError());
+    if ((rc = launch_ex(ctx, residual_norm_kernel, dim3(1), dim3(kDecodeThreads), 0, st, true, m->x,
+                        static_cast<const uint16_t*>(m->proj), H, static_cast<const float*>(m->norms + (2 * l + 2) * H),
+                        eps, m->xn)))
+      return rc;
   }
   if (logits && (rc = gemv_into(ctx, m, m->lm, m->xn, m->logits, st))) return rc;
-  argmax_advance_kernel<<<1, kDecodeThreads, 0, st>>>(logits ? m->logits : nullptr, c.vocab, m->state, m->tokens);
-  ALV_CUDA(ctx, cudaGetLastError());
+  if ((rc = launch_ex(ctx, argmax_advance_kernel, dim3(1), dim3(kDecodeThreads), 0, st, true,
+                      static_cast<const uint16_t*>(logits ? m->logits : nullptr), c.vocab, m->state, m->tokens,
+                      m->pred)))
+    return rc;
   return ALV_OK;
 }
 
@@ -300,7 +306,8 @@ extern "C" int alv_llama_create(alv_ctx* ctx, const alv_llama_config* cfg, alv_h
       (rc = model_alloc(ctx, m, &m->vcache, m->kv_elems() * 2)) ||
       (rc = model_alloc(ctx, m, &m->act16, align_up(acts, 8) * 2 + 1024)) ||
       (rc = model_alloc(ctx, m, &m->state, sizeof(DecodeState))) ||
-      (rc = model_alloc(ctx, m, &m->tokens, (static_cast<size_t>(c.max_seq) + 1) * 4))) {
+      (rc = model_alloc(ctx, m, &m->tokens, (static_cast<size_t>(c.max_seq) + 1) * 4)) ||
+      (rc = model_alloc(ctx, m, &m->pred, (static_cast<size_t>(c.max_seq) + 1) * 4))) {
     free_model(m);
     w->model = nullptr;
     return rc;
@@ -320,6 +327,7 @@ extern "C" int alv_llama_create(alv_ctx* ctx, const alv_llama_config* cfg, alv_h
   m->proj = take(H);
   m->logits = take(c.vocab);
   cudaMemset(m->tokens, 0, (static_cast<size_t>(c.max_seq) + 1) * 4);
+  cudaMemset(m->pred, 0, (static_cast<size_t>(c.max_seq) + 1) * 4);
   cudaMemset(m->state, 0, sizeof(DecodeState));
   *out = add_weight(ctx, std::move(w));
   return ALV_OK;
@@ -432,7 +440,8 @@ extern "C" int alv_llama_run(alv_ctx* ctx, alv_handle h, int n_prompt_steps, int
   return ALV_OK;
 }
 
-extern "C" int alv_llama_tokens(alv_ctx* ctx, alv_handle h, int first, int n, int32_t* out_host, void* stream) {
+namespace {
+int copy_ids(alv_ctx* ctx, alv_handle h, bool predicted, int first, int n, int32_t* out_host, void* stream) {
   if (!ctx || !out_host || first < 0 || n < 0) return fail(ctx, ALV_ERR_ARG, "llama_tokens: bad argument");
   LlamaModel* m = get_model(ctx, h);
   if (!m) return fail(ctx, ALV_ERR_HANDLE, "llama_tokens: invalid handle (not a llama model)");
@@ -440,8 +449,18 @@ extern "C" int alv_llama_tokens(alv_ctx* ctx, alv_handle h, int first, int n, in
   int rc = set_device(ctx);
   if (rc) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  ALV_CUDA(ctx, cudaMemcpyAsync(out_host, m->tokens + first, static_cast<size_t>(n) * 4, cudaMemcpyDeviceToHost, st));
+  ALV_CUDA(ctx, cudaMemcpyAsync(out_host, (predicted ? m->pred : m->tokens) + first, static_cast<size_t>(n) * 4,
+                                cudaMemcpyDeviceToHost, st));
   return check_status(ctx, st);
+}
+}  // namespace
+
+extern "C" int alv_llama_tokens(alv_ctx* ctx, alv_handle h, int first, int n, int32_t* out_host, void* stream) {
+  return copy_ids(ctx, h, false, first, n, out_host, stream);
+}
+
+extern "C" int alv_llama_predicted(alv_ctx* ctx, alv_handle h, int first, int n, int32_t* out_host, void* stream) {
+  return copy_ids(ctx, h, true, first, n, out_host, stream);
 }
 
 extern "C" int alv_llama_generate(alv_ctx* ctx, alv_handle h, const int32_t* prompt, int n_prompt, int steps,

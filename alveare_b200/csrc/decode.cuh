@@ -81,6 +81,8 @@ __global__ void __launch_bounds__(kDecodeThreads) embed_norm_kernel(const uint16
                                                                     uint16_t* __restrict__ x,
                                                                     uint16_t* __restrict__ xn) {
   __shared__ float red[32];
+  pdl_wait();
+  pdl_trigger();
   const int tok = tokens[st->pos];
   const uint16_t* row = emb + static_cast<size_t>(tok) * H;
   float xv[kDecodePer];
@@ -103,6 +105,8 @@ __global__ void __launch_bounds__(kDecodeThreads) residual_norm_kernel(uint16_t*
                                                                        const float* __restrict__ w, float eps,
                                                                        uint16_t* __restrict__ xn) {
   __shared__ float red[32];
+  pdl_wait();
+  pdl_trigger();
   float xv[kDecodePer];
 #pragma unroll
   for (int i = 0; i < kDecodePer; ++i) {
@@ -132,6 +136,8 @@ struct RopeParams {
 };
 
 __global__ void __launch_bounds__(kDecodeThreads) rope_cache_kernel(const RopeParams p) {
+  pdl_wait();
+  pdl_trigger();
   const int pos = p.st->pos;
   const int half = p.hd / 2;
   const uint16_t* cs = p.table + static_cast<size_t>(pos) * 2 * p.hd;
@@ -179,6 +185,8 @@ struct AttnParams {
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParams p) {
   extern __shared__ float sm[];          // [hd] q, [max_seq] scores, [blockDim / hd][hd] partial outputs
   __shared__ float red[32];
+  pdl_wait();
+  pdl_trigger();
   const int head = blockIdx.x, kvh = head / (p.nq / p.nkv);
   const int seq = p.st->pos + 1;
   float* qs = sm;
@@ -231,12 +239,16 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
   }
 }
 
-// End of a step: with logits, tokens[pos+1] = argmax (the first index of
-// the maximum, as np.argmax); then pos += 1 (the next step's position).
+// End of a step: with logits, pred[pos+1] = argmax (the first index of the
+// maximum, as np.argmax), which also becomes tokens[pos+1] unless that
+// position holds a prompt token (then the prediction is only recorded: a
+// teacher-forced run); then pos += 1 (the next step's position).
 __global__ void __launch_bounds__(kDecodeThreads) argmax_advance_kernel(const uint16_t* __restrict__ logits, int V,
-                                                                        DecodeState* st, int* tokens) {
+                                                                        DecodeState* st, int* tokens, int* pred) {
   __shared__ float rv[32];
   __shared__ int ri[32];
+  pdl_wait();
+  pdl_trigger();
   const int pos = st->pos;
   if (logits) {
     float best = -INFINITY;
@@ -269,7 +281,8 @@ __global__ void __launch_bounds__(kDecodeThreads) argmax_advance_kernel(const ui
           best = rv[w];
           bi = ri[w];
         }
-      tokens[pos + 1] = bi;
+      pred[pos + 1] = bi;
+      if (pos + 1 >= st->n_prompt) tokens[pos + 1] = bi;
     }
   }
   if (threadIdx.x == 0) st->pos = pos + 1;

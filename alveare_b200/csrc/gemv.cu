@@ -6,7 +6,7 @@ namespace alv {
 namespace {
 
 template <int NCOLS, bool SPLIT, bool FAST>
-int launch_gemv_t(alv_ctx* ctx, GemvParams p, cudaStream_t st) {
+int launch_gemv_t(alv_ctx* ctx, GemvParams p, cudaStream_t st, bool pdl) {
   const size_t other = part_bytes(p.x.ntok) + frag_bytes(p.m.KT, NCOLS);
   p.nst = ring_stages(other);
   if (!p.nst) return fail(ctx, ALV_ERR_UNSUPPORTED, "gemv: K too large for the shared-memory fragment stage");
@@ -16,27 +16,25 @@ int launch_gemv_t(alv_ctx* ctx, GemvParams p, cudaStream_t st) {
   // to arrive), so a plain launch is enough; one CTA per SM.
   int rc = prepare_kernel(ctx, k, smem);
   if (rc) return rc;
-  k<<<ctx->num_sms, kThreadsPerCta, smem, st>>>(p);
-  ALV_CUDA(ctx, cudaGetLastError());
-  return ALV_OK;
+  return launch_ex(ctx, k, dim3(ctx->num_sms), dim3(kThreadsPerCta), smem, st, pdl, p);
 }
 
 template <bool FAST>
-int launch_gemv_f(alv_ctx* ctx, const GemvParams& p, bool split, uint32_t ncols, cudaStream_t st) {
+int launch_gemv_f(alv_ctx* ctx, const GemvParams& p, bool split, uint32_t ncols, cudaStream_t st, bool pdl) {
   if (split) {
     switch (ncols) {
-      case 2: return launch_gemv_t<2, true, FAST>(ctx, p, st);
-      case 4: return launch_gemv_t<4, true, FAST>(ctx, p, st);
-      case 8: return launch_gemv_t<8, true, FAST>(ctx, p, st);
-      case 16: return launch_gemv_t<16, true, FAST>(ctx, p, st);
+      case 2: return launch_gemv_t<2, true, FAST>(ctx, p, st, pdl);
+      case 4: return launch_gemv_t<4, true, FAST>(ctx, p, st, pdl);
+      case 8: return launch_gemv_t<8, true, FAST>(ctx, p, st, pdl);
+      case 16: return launch_gemv_t<16, true, FAST>(ctx, p, st, pdl);
     }
   } else {
     switch (ncols) {
-      case 1: return launch_gemv_t<1, false, FAST>(ctx, p, st);
-      case 2: return launch_gemv_t<2, false, FAST>(ctx, p, st);
-      case 4: return launch_gemv_t<4, false, FAST>(ctx, p, st);
-      case 8: return launch_gemv_t<8, false, FAST>(ctx, p, st);
-      case 16: return launch_gemv_t<16, false, FAST>(ctx, p, st);
+      case 1: return launch_gemv_t<1, false, FAST>(ctx, p, st, pdl);
+      case 2: return launch_gemv_t<2, false, FAST>(ctx, p, st, pdl);
+      case 4: return launch_gemv_t<4, false, FAST>(ctx, p, st, pdl);
+      case 8: return launch_gemv_t<8, false, FAST>(ctx, p, st, pdl);
+      case 16: return launch_gemv_t<16, false, FAST>(ctx, p, st, pdl);
     }
   }
   return fail(ctx, ALV_ERR_UNSUPPORTED, "unsupported column count");
@@ -66,8 +64,9 @@ GemvParams gemv_params(Weight* w, int ntok, const void* x, int x_dtype, void* y,
 
 }  // namespace
 
-int launch_gemv_params(alv_ctx* ctx, const GemvParams& p, bool split, uint32_t ncols, cudaStream_t st) {
-  return p.m.fast ? launch_gemv_f<true>(ctx, p, split, ncols, st) : launch_gemv_f<false>(ctx, p, split, ncols, st);
+int launch_gemv_params(alv_ctx* ctx, const GemvParams& p, bool split, uint32_t ncols, cudaStream_t st, bool pdl) {
+  return p.m.fast ? launch_gemv_f<true>(ctx, p, split, ncols, st, pdl)
+                  : launch_gemv_f<false>(ctx, p, split, ncols, st, pdl);
 }
 
 int do_gemv(alv_ctx* ctx, Weight* w, int ntok, const void* x, int x_dtype, void* y, int y_dtype,

@@ -214,6 +214,26 @@ int launch_cooperative(alv_ctx* ctx, void (*kernel)(P), const P& p, unsigned gri
   return ALV_OK;
 }
 
+// Launch `kernel`; with `pdl` as a programmatic dependent launch (it may
+// start while its predecessor in the stream finishes; the kernel calls
+// pdl_wait() before it touches that predecessor's data).
+template <class... KArgs, class... Args>
+int launch_ex(alv_ctx* ctx, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+              Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  ALV_CUDA(ctx, cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+  return ALV_OK;
+}
+
 // Ring stages per warp that fit beside `other` bytes of dynamic shared memory
 // (at most kMaxStages), leaving room for the kernels' static shared memory
 // (per-warp work lists and copy cursors, < kStaticSmemReserve bytes).

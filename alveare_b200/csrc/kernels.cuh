@@ -225,6 +225,51 @@ inline __device__ bool grid_barrier_epoch(GridBar* gb, uint32_t nblocks, unsigne
   return consumers_and(ok != 0);
 }
 
+// Exchange step of a tensor-parallel FFN stack (ranks on distinct GPUs, one
+// launch each), after the rank's own grid barrier: CTA 0 -- which the grid
+// barrier ordered after every local CTA's pushes -- issues one system-scope
+// release (fence.acq_rel.sys) and adds 1 to every rank's counter, its own
+// included; every CTA then polls its own counter (system-scope acquire) for
+// base + epoch * world.  One system fence per rank and exchange, not one per
+// CTA.  `base` is the own counter at launch rounded down to a multiple of
+// world: before this launch's CTA 0 signals (which needs every local CTA past
+// the first grid barrier, so after each CTA read its base) at most the
+// other ranks' world - 1 first-exchange signals can have landed.
+__device__ __forceinline__ unsigned long long peer_base(const uint8_t* own, uint32_t world) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(own) : "memory");
+  return v / world * world;
+}
+inline __device__ bool peer_exchange(uint8_t* const* xr, uint32_t world, uint32_t rank, unsigned long long base,
+                              uint32_t epoch, uint32_t* status) {
+  int ok = 1;
+  if (threadIdx.x == 0) {
+    if (blockIdx.x == 0) {
+      asm volatile("fence.acq_rel.sys;" ::: "memory");
+      for (uint32_t q = 0; q < world; ++q)
+        asm volatile("red.relaxed.sys.global.add.u64 [%0], 1;" ::"l"(xr[q]) : "memory");
+    }
+    const unsigned long long target = base + static_cast<unsigned long long>(epoch) * world;
+    const uint8_t* own = xr[rank];
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(own) : "memory");
+    if (v < target) {
+      const unsigned long long t0 = globaltimer_ns();
+      while (true) {
+        asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(own) : "memory");
+        if (v >= target) break;
+        if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+          atomicOr(status, kStatusPeerTimeout);
+          ok = 0;
+          break;
+        }
+      }
+    }
+  }
+  return consumers_and(ok != 0);
+}
+
+
 // Sum over the consumer threads (all of them get the result) through `red`
 // (>= 16 floats).  One named barrier: consecutive calls must alternate
 // between two such buffers (a call's buffer is rewritten two calls later,
@@ -288,7 +333,10 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) gemv_kernel(const GemvParam
   __shared__ WorkList wl[kConsumerWarps];
   __shared__ uint32_t wr[kConsumerWarps][4];  // per warp: unit range [u0, u1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const Partition pt = Partition::make(p.m.RT, p.m.KT, gridDim.x);
+  // Row-aligned unless there are too few row tiles to keep the SMs busy: a
+  // row tile split between CTAs costs the finishing CTA a fence, an atomic
+  // and a round trip at the end, more than the imbalance of whole rows.
+  const Partition pt = Partition::make(p.m.RT, p.m.KT, gridDim.x, p.m.RT * 4 >= gridDim.x);
   Shape::init_barriers(smem, p.nst);
   uint64_t w0, w1;
   pt.warp_range(blockIdx.x, warp, w0, w1);
@@ -300,11 +348,13 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) gemv_kernel(const GemvParam
     wr[warp][1] = u1;
   }
   __syncthreads();
+  pdl_trigger();
   ConsumerRing<kUnitsPerStage, WorkList> ring;
   ring.setup(smem, p.nst, warp, u1 - u0, &wl[warp]);  // weights start streaming
   Fixup fx = p.fx;
   fx.part = reinterpret_cast<float*>(smem + ring_smem_bytes(p.nst));
   uint8_t* xs = smem + base_smem_bytes(p.nst, p.x.ntok);
+  pdl_wait();  // x, y and the split-K workspace belong to the stream's order from here
   stage_frags<NCOLS, SPLIT>(xs, p.m.KT, p.x);
   consumers_sync();
   if (!consume_range<NCOLS, SPLIT, FAST>(ring, p.m, u0, u1, xs, fx, p.x.ntok, p.epi, p.status))
@@ -371,6 +421,80 @@ struct F32In {    // fp32 values in memory written before the launch (or shared)
   __device__ __forceinline__ float operator()(uint32_t, uint32_t, size_t i) const { return p[i]; }
   __device__ __forceinline__ void load(uint32_t, uint32_t, size_t i, float& a, float& b, uint32_t& how) const {
     a = p[i];
+    b = 0.f;
+    how = 0;
+  }
+  __device__ __forceinline__ float combine(float a, float, uint32_t) const { return a; }
+};
+// The down projection of the previous stack layer as the glue reads it
+// (token tok, index h, flat i = tok*H + h): a row tile held by one CTA is
+// final in `down`; a row tile split between CTAs was left as CTA partials
+// (cta_fixup<true>) that are summed here in CTA order and scaled, exactly as
+// the last CTA to arrive would have done.  split[r] = element offsets in ws
+// of the first two CTAs' partials of row tile r (x = ~0: not split), or
+// y = ~0 with x = the first CTA when the tile spans three or more CTAs.
+struct DownIn {
+  const float* down;
+  const float* ws;          // CTA partials: [CTA][2 slots][ntok][16]
+  const uint2* split;       // per row tile, see above
+  const uint32_t* cfirst;   // per CTA: its first row tile
+  const uint32_t* span;     // per row tile: first CTA | last CTA << 16
+  uint32_t slot_floats;
+  float sm;
+  // Two passes, so a thread's loads are all in flight before any is used:
+  // load() issues them, combine() adds and scales.
+  __device__ __forceinline__ void load(uint32_t tok, uint32_t h, size_t i, float& a, float& b, uint32_t& how) const {
+    const uint32_t r = h >> 4;
+    const uint2 o = split[r];
+    const uint32_t e = tok * 16 + (h & 15);
+    if (o.x == ~0u) {
+      a = __ldcg(down + i);
+      b = 0.f;
+      how = 0;
+    } else if (o.y != ~0u) {
+      a = __ldcg(ws + o.x + e);
+      b = __ldcg(ws + o.y + e);
+      how = 1;
+    } else {  // a row tile over three or more CTAs (small problems)
+      const uint32_t sp = span[r];
+      float v = 0.f;
+      for (uint32_t c = sp & 0xFFFFu; c <= (sp >> 16); ++c)
+        v += __ldcg(ws + (static_cast<size_t>(c) * 2 + (r == cfirst[c] ? 0 : 1)) * slot_floats + e);
+      a = v;
+      b = 0.f;
+      how = 2;
+    }
+  }
+  __device__ __forceinline__ float combine(float a, float b, uint32_t how) const {
+    return how == 0 ? a : (how == 1 ? (a + b) * sm : a * sm);
+  }
+};
+// The down projection of a tensor-parallel layer: the sum over ranks, in
+// rank order, of each rank's DownIn (whole rows and CTA partials, all
+// pre-scaled) as the ranks pushed them into this GPU's exchange slots.
+// Every rank sums the same values in the same order, so every rank's
+// residual stream is identical.
+struct DownInX {
+  const float* slot0;       // this parity's slot of rank 0 (local memory)
+  uint32_t stride;          // floats from one rank's slot to the next
+  uint32_t world;
+  uint32_t ws_off;          // CTA partials within a slot
+  const uint2* split;
+  const uint32_t* cfirst;
+  const uint32_t* span;
+  uint32_t slot_floats;
+  __device__ __forceinline__ void load(uint32_t tok, uint32_t h, size_t i, float& a, float& b, uint32_t& how) const {
+    float v = 0.f;
+    for (uint32_t q = 0; q < world; ++q) {
+      const float* d = slot0 + static_cast<size_t>(q) * stride;
+      const DownIn di{d, d + ws_off, split, cfirst, span, slot_floats, 1.0f};
+      float x, y;
+      uint32_t hw;
+      di.load(tok, h, i, x, y, hw);
+      const float t = di.combine(x, y, hw);
+      v = q ? v + t : t;
+    }
+    a = v;
     b = 0.f;
     how = 0;
   }
@@ -554,8 +678,10 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_kernel(const FfnParams 
     bulk_g2s(xraw, p.x_in, xb, xbar, pol);
     if (db) bulk_g2s(draw, p.down_in, db, xbar, pol);
   }
+  pdl_trigger();
   ConsumerRing<kUnitsPerStage, WorkList> ring;
   ring.setup(smem, p.nst, warp, (a1 - a0) + (b1 - b0), &wl[warp]);
+  pdl_wait();
   trace_mark(p.trace, 0);
 
   // The act padding (k in [I, 64*dn.KT)) must read as zero in phase B.
@@ -634,111 +760,42 @@ struct StackParams {
   float eps;
   const uint16_t* x_in;   // [ntok][H] bf16 stack input
   uint16_t* out;          // [ntok][H] bf16 stack output
+  float* down;            // [ntok][H] fp32: a layer's down projection
   uint8_t* act;           // [dn.KT*64][ntok] bf16 intermediate, B-fragment order
-  Fixup fxA;
+  Fixup fxA, fxB;
   GridBar* bar;
   uint32_t* status;
   uint32_t nst;
   unsigned long long* trace;  // optional: phase stamps of layer 1
   float* probe;               // optional: [ntok][H] fp32 down projection of the last layer
-  // Exchange of each layer's down projection (see ffn_stack_kernel):
-  // xr[q] is rank q's exchange region as mapped on this GPU (xr[rank] is
-  // this GPU's own; one rank without tensor parallelism):
-  //   [header: launch counter u64 @0, kXHeader bytes]
-  //   [slots: parity x world x slot_words LL words]
-  // Slot (parity, owner) holds rank `owner`'s down output of the layers of
-  // that parity: [whole rows: ntok x H @0][CTA partials: #CTAs x 2 x ntok x 16 @rows_words].
+  // Tensor parallelism (ffn_stack_kernel<..., TP = true>): rank `rank` of
+  // `world` holds an I-slice of every layer.  xr[q] is rank q's exchange
+  // region as mapped on this GPU (xr[rank] is this GPU's own):
+  //   [peer-barrier counter u64 @0][slots @kXHeader: parity x world x xslot floats]
+  // Slot (parity, q) of every region holds rank q's down output of the
+  // layers of that parity: [whole rows: ntok x H][CTA partials @xws_off].
   uint32_t world, rank;
   uint8_t* xr[kMaxRanks];
-  uint32_t slot_words, rows_words;
+  uint32_t xslot, xws_off;
 };
 
-// Exchange region header (the launch counter), padded.
+// Exchange region header: the peer-barrier counter, padded.
 constexpr size_t kXHeader = 256;
 
-// ---------------------------------------------------------------------------
-// LL words: a float and the epoch (layer of a launch) it belongs to, stored
-// and loaded as one aligned 64-bit access, so a reader that sees the epoch
-// sees the value -- no fence, counter or barrier between writer and reader.
-// SYS: system scope (peer GPUs write into this memory over NVLink).
-// ---------------------------------------------------------------------------
-template <bool SYS>
-__device__ __forceinline__ void ll_store(unsigned long long* p, float v, uint32_t epoch) {
-  const unsigned long long w = (static_cast<unsigned long long>(epoch) << 32) | __float_as_uint(v);
-  if (SYS)
-    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
-  else
-    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
-}
-template <bool SYS>
-__device__ __forceinline__ ulonglong2 ll_load2(const unsigned long long* p) {  // two words, 16-byte aligned
-  ulonglong2 w;
-  if (SYS)
-    asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];" : "=l"(w.x), "=l"(w.y) : "l"(p) : "memory");
-  else
-    asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(w.x), "=l"(w.y) : "l"(p) : "memory");
-  return w;
-}
-template <bool SYS>
-__device__ __forceinline__ unsigned long long ll_load1(const unsigned long long* p) {
-  unsigned long long w;
-  if (SYS)
-    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
-  else
-    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
-  return w;
-}
-__device__ __forceinline__ uint32_t ll_epoch(unsigned long long w) { return static_cast<uint32_t>(w >> 32); }
-__device__ __forceinline__ float ll_value(unsigned long long w) { return __uint_as_float(static_cast<uint32_t>(w)); }
-
-// Re-read a word until it carries `epoch`; false after kWaitTimeoutNs.
-template <bool SYS>
-__device__ __noinline__ bool ll_wait(const unsigned long long* p, uint32_t epoch, unsigned long long& w) {
-  const unsigned long long t0 = globaltimer_ns();
-  while (true) {
-    w = ll_load1<SYS>(p);
-    if (ll_epoch(w) == epoch) return true;
-    if (globaltimer_ns() - t0 > kWaitTimeoutNs) return false;
-  }
-}
-
-// Epoch of layer l of the launch whose counter read `seq`: never 0 (the
-// value of a never-written word).
-__device__ __forceinline__ uint32_t layer_epoch(unsigned long long seq, uint32_t L, uint32_t l) {
-  return static_cast<uint32_t>((seq * L + l) % 0xFFFFFFFFull) + 1u;
-}
-
-__device__ __forceinline__ unsigned long long* xslot(const StackParams& p, uint32_t region, uint32_t par,
-                                                     uint32_t owner) {
-  return reinterpret_cast<unsigned long long*>(p.xr[region] + kXHeader) +
-         (static_cast<size_t>(par) * p.world + owner) * p.slot_words;
-}
-
 // Epilogue of either stack phase: gate/up -> activation into act (phase A),
-// or down rows (whole) and CTA partials (rows shared with other CTAs) as LL
-// words into this rank's slot of every rank's exchange region (phase B).
-template <bool SYS>
+// or down rows into the fp32 down vector (phase B).
 struct StackEpi {
   bool down_phase;
   uint8_t* act;
-  const StackParams* sp;
-  uint32_t par, epoch;
+  float* down;
   uint32_t I, H, ncb;
   float sm;
   int fn;
-  float pmul;  // parked partials are stored times pmul (1, or sm when the sum is taken across ranks)
-  __device__ __forceinline__ void put_word(size_t off, float v) const {
-    for (uint32_t q = 0; q < sp->world; ++q) ll_store<SYS>(xslot(*sp, q, par, sp->rank) + off, v, epoch);
-  }
-  __device__ __forceinline__ void park(uint32_t cta, int cslot, uint32_t e, float v) const {
-    put_word(sp->rows_words + (static_cast<size_t>(cta) * 2 + cslot) * (static_cast<uint32_t>(sp->ntok) * 16) + e,
-             v * pmul);
-  }
+  float pmul;  // parked CTA partials are stored times pmul (1, or sm when the sum is taken across ranks)
+  __device__ __forceinline__ float park(float v) const { return v * pmul; }
   __device__ __forceinline__ void apply(uint32_t r, int g, int tok, float vg, float vg8) const {
     if (down_phase) {
-      const uint32_t row = r * 16 + g;
-      if (row < H) put_word(static_cast<size_t>(tok) * H + row, vg * sm);
-      if (row + 8 < H) put_word(static_cast<size_t>(tok) * H + row + 8, vg8 * sm);
+      RowsEpi{down, nullptr, H, H, sm}.apply(r, g, tok, vg, vg8);
     } else {
       GateUpEpi{act, I, ncb, sm, fn}.apply(r, g, tok, vg, vg8);
     }
@@ -747,7 +804,7 @@ struct StackEpi {
 
 // Shared layout after the rings: [xs region][red 32 f][xres ntok*H bf16].
 // The xs region holds phase B's fragments, or phase A's fragments followed by
-// the gathered down projection (dsum, fp32 [ntok][H]) that the glue reads.
+// the glue's xn (tmp, fp32).
 __host__ __device__ inline size_t stack_xs_region(uint32_t KTA, uint32_t KTB, int nc, uint32_t H, int ntok) {
   const size_t b = frag_bytes(KTB, nc);
   const size_t a = frag_bytes(KTA, nc) + static_cast<size_t>(ntok) * H * 4;
@@ -764,140 +821,57 @@ __host__ __device__ inline size_t stack_smem_bytes(uint32_t nst, uint32_t KTA, u
   return stack_tables_offset(nst, KTA, KTB, nc, H, ntok) + (static_cast<size_t>(RTB) * 3 + nctas) * 4;
 }
 
-// Wait for and sum the previous layer's down projection into dsum (fp32
-// [ntok][H], before the glue's bf16 rounding): per element, each rank's
-// value -- a whole row's word, or its CTA partials summed in CTA order
-// (scaled by `smul` unless the ranks pre-scaled them) -- summed over the
-// ranks in rank order, the arithmetic of the last-arriver fix-up of the
-// per-layer kernel.  Element pairs (h, h+1) are read as 16-byte loads; W
-// ranks at a time keep 16 such loads in flight per thread.  Returns false
-// (and sets `timeout_bit`) when a word did not arrive in time.
-template <int W, bool SYS>
-__device__ bool ll_gather(const StackParams& p, uint32_t par, uint32_t epoch, float smul, const uint2* split,
-                          const uint32_t* cfirst, const uint32_t* span, float* dsum, uint32_t timeout_bit) {
+// Slot (parity, owner) of rank `region`'s exchange region (TP stacks).
+__device__ __forceinline__ float* xslot_ptr(const StackParams& p, uint32_t region, uint32_t par, uint32_t owner) {
+  return reinterpret_cast<float*>(p.xr[region] + kXHeader) + (static_cast<size_t>(par) * p.world + owner) * p.xslot;
+}
+
+// Tensor parallelism: copy what this CTA wrote into its own rank's slot --
+// its whole down rows [row0, row1) and its two CTA-partial slots -- to the
+// same offsets of every peer's slot (plain stores over NVLink, consecutive
+// threads on consecutive floats).
+inline __device__ void push_down(const StackParams& p, uint32_t par, uint32_t row0, uint32_t row1) {
   constexpr uint32_t NTHR = kConsumerWarps * 32;
-  constexpr int C = W >= 8 ? 1 : 8 / W;    // element pairs per batch
+  consumers_sync();  // every warp's rows and partials are written
+  const float* src = xslot_ptr(p, p.rank, par, p.rank);
   const uint32_t H = p.H, ntok = static_cast<uint32_t>(p.ntok);
-  const uint32_t npairs = ntok * H / 2, sw = ntok * 16;
-  bool ok = true;
-  for (uint32_t base = threadIdx.x; base < npairs; base += NTHR * C) {
-    ulonglong2 w[C][W][2];
-    uint32_t kind[C];     // 0 whole row, 1 two CTA partials, 2 three or more (slow path)
-    uint32_t off0[C], off1[C];
-#pragma unroll
-    for (int j = 0; j < C; ++j) {
-      const uint32_t pr = base + j * NTHR;
-      kind[j] = 3;        // beyond the end
-      if (pr >= npairs) continue;
-      const uint32_t e = 2 * pr, tok = e / H, h = e - tok * H, r = h >> 4;
-      const uint2 o = split[r];
-      const uint32_t el = tok * 16 + (h & 15);
-      if (o.x == ~0u) {
-        kind[j] = 0;
-        off0[j] = e;
-        off1[j] = 0;
-      } else if (o.y != ~0u) {
-        kind[j] = 1;
-        off0[j] = p.rows_words + o.x + el;
-        off1[j] = p.rows_words + o.y + el;
-      } else {
-        kind[j] = 2;
-        off0[j] = r;
-        off1[j] = el;
-      }
-#pragma unroll
-      for (int q = 0; q < W; ++q) {
-        const unsigned long long* s = xslot(p, p.rank, par, q);
-        if (kind[j] <= 1) w[j][q][0] = ll_load2<SYS>(s + off0[j]);
-        if (kind[j] == 1) w[j][q][1] = ll_load2<SYS>(s + off1[j]);
-      }
+  const uint32_t h0 = min(row0 * 16, H), h1 = min(row1 * 16, H), nr = h1 - h0;
+  const uint32_t sf = ntok * 16, n_rows = nr * ntok, n = n_rows + 2 * sf;
+  for (uint32_t e = threadIdx.x; e < n; e += NTHR) {
+    size_t off;
+    if (e < n_rows) {
+      const uint32_t tok = e / nr;
+      off = static_cast<size_t>(tok) * H + h0 + (e - tok * nr);
+    } else {
+      off = p.xws_off + static_cast<size_t>(blockIdx.x) * 2 * sf + (e - n_rows);
     }
-#pragma unroll
-    for (int j = 0; j < C; ++j) {
-      if (kind[j] == 3) continue;
-      const uint32_t e = 2 * (base + j * NTHR);
-      float acc0 = 0.f, acc1 = 0.f;
-#pragma unroll
-      for (int q = 0; q < W; ++q) {
-        const unsigned long long* s = xslot(p, p.rank, par, q);
-        float t0, t1;
-        if (kind[j] == 2) {  // a row tile over three or more CTAs: sequential waits
-          const uint32_t r = off0[j], el = off1[j], sp = span[r];
-          t0 = t1 = 0.f;
-          for (uint32_t c = sp & 0xFFFFu; c <= (sp >> 16); ++c) {
-            const unsigned long long* a = s + p.rows_words + (static_cast<size_t>(c) * 2 + (r == cfirst[c] ? 0 : 1)) * sw + el;
-            unsigned long long x0, x1;
-            ok = ll_wait<SYS>(a, epoch, x0) && ll_wait<SYS>(a + 1, epoch, x1) && ok;
-            t0 += ll_value(x0);
-            t1 += ll_value(x1);
-          }
-          t0 *= smul;
-          t1 *= smul;
-        } else {
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            if (h == 1 && kind[j] == 0) break;
-            ulonglong2& v = w[j][q][h];
-            const unsigned long long* a = s + (h ? off1[j] : off0[j]);
-            if (ll_epoch(v.x) != epoch) ok = ll_wait<SYS>(a, epoch, v.x) && ok;
-            if (ll_epoch(v.y) != epoch) ok = ll_wait<SYS>(a + 1, epoch, v.y) && ok;
-          }
-          if (kind[j] == 0) {
-            t0 = ll_value(w[j][q][0].x);
-            t1 = ll_value(w[j][q][0].y);
-          } else {
-            t0 = (ll_value(w[j][q][0].x) + ll_value(w[j][q][1].x)) * smul;
-            t1 = (ll_value(w[j][q][0].y) + ll_value(w[j][q][1].y)) * smul;
-          }
-        }
-        acc0 = q ? acc0 + t0 : t0;
-        acc1 = q ? acc1 + t1 : t1;
-      }
-      dsum[e] = acc0;
-      dsum[e + 1] = acc1;
-    }
-  }
-  if (!ok) atomicOr(p.status, timeout_bit);
-  return consumers_and(ok);
-}
-
-template <bool SYS>
-__device__ __forceinline__ bool ll_gather_any(const StackParams& p, uint32_t par, uint32_t epoch, float smul,
-                                              const uint2* split, const uint32_t* cfirst, const uint32_t* span,
-                                              float* dsum, uint32_t timeout_bit) {
-  switch (p.world) {
-    case 1: return ll_gather<1, SYS>(p, par, epoch, smul, split, cfirst, span, dsum, timeout_bit);
-    case 2: return ll_gather<2, SYS>(p, par, epoch, smul, split, cfirst, span, dsum, timeout_bit);
-    case 4: return ll_gather<4, SYS>(p, par, epoch, smul, split, cfirst, span, dsum, timeout_bit);
-    default: return ll_gather<8, SYS>(p, par, epoch, smul, split, cfirst, span, dsum, timeout_bit);
+    const float v = __ldcg(src + off);
+    for (uint32_t q = 0; q < p.world; ++q)
+      if (q != p.rank) xslot_ptr(p, q, par, p.rank)[off] = v;
   }
 }
 
-// ===========================================================================
-// Whole FFN stack in one persistent launch: for l = 0..L-1
-//   glue (x += rmsnorm(down_{l-1}); xn = rmsnorm(x)) -> phase A (gate/up +
-//   activation -> act) -> grid barrier -> phase B (down -> LL words),
-// then the last residual x += rmsnorm(down_{L-1}) -> out.  Each warp's ring
-// runs through every layer's weights back to back, so nst groups stay in
-// flight while the warps run the glue and wait.  The residual stream stays
-// in shared memory (every CTA holds the identical copy); act crosses CTAs
-// through L2 behind the grid barrier, and each layer's down projection as
-// epoch-tagged LL words that the next glue polls, so no barrier follows
-// phase B.  The gate/up partition is row-aligned (no cross-CTA partials),
-// the down partition unit-balanced (rows split between CTAs leave partials
-// that the glue sums in CTA order).  Arithmetic and reduction order equal
-// the per-layer ffn_kernel chain, so the two paths agree bit for bit.
-//
-// TP = true: rank `rank` of `world` holds an I-slice of every layer and
-// writes its partial down rows and CTA partials (pre-scaled) into its slot
-// of every rank's exchange region over NVLink (system-scope LL words);
-// every rank's glue sums the ranks' slots in rank order, so every rank's
-// residual stream is identical.  Slots alternate between two parities by
-// layer: a rank can only write layer l+2 after every rank finished reading
-// layer l (it needs their layer l+1 first).  Epochs come from a launch
-// counter in the region header that CTA 0 advances at the end of a launch,
-// so words of earlier launches never match.
-// ===========================================================================
+// The last layer's down projection as the final glue read it (fp32, summed
+// over CTAs and, with tensor parallelism, over ranks): a test probe.
+template <class DL>
+__device__ void write_probe(float* probe, int ntok, uint32_t H, const DL& dl) {
+  const uint32_t n = static_cast<uint32_t>(ntok) * H;
+  for (uint32_t e = threadIdx.x; e < n; e += kConsumerWarps * 32) {
+    const uint32_t tok = e / H, h = e - tok * H;
+    float a, b;
+    uint32_t how;
+    dl.load(tok, h, e, a, b, how);
+    probe[e] = dl.combine(a, b, how);
+  }
+}
+
+// TP = true: one rank of a tensor-parallel stack (see StackParams).  Phase B
+// writes this rank's partial down projection into its own exchange slot and
+// pushes it to every peer; after the rank's grid barrier the ranks meet in
+// peer_exchange, and the next glue sums the ranks' slots in rank order.  The
+// slots alternate between two parities by the global count of exchanges, so
+// a rank that runs ahead writes the other parity from the one its peers
+// still read.
 template <int NT, bool FAST, bool TP>
 __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const __grid_constant__ StackParams p) {
   constexpr int NC = NT;  // bf16 activations: one fragment column per token
@@ -905,14 +879,13 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const __gr
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint32_t wk[kConsumerWarps][4];  // per warp: a0 a1 b0 b1
   __shared__ StackWork sw[kConsumerWarps];
-  __shared__ unsigned long long seq_s;
+  __shared__ unsigned long long xbase_s;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const Partition ptA = Partition::make(p.gu.RT, p.gu.KT, gridDim.x, true);
   const Partition ptB = Partition::make(p.dn.RT, p.dn.KT, gridDim.x);
   Shape::init_barriers(smem, p.nst);
   const unsigned long long bar_base = threadIdx.x == 0 ? grid_base(p.bar, gridDim.x) : 0ull;
-  unsigned long long* seq_ptr = reinterpret_cast<unsigned long long*>(p.xr[p.rank]);
-  if (threadIdx.x == 0) asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(seq_s) : "l"(seq_ptr) : "memory");
+  if (TP && threadIdx.x == 0) xbase_s = peer_base(p.xr[p.rank], p.world);
   if (lane == 0) {
     uint64_t a0, a1, b0, b1;
     ptA.warp_range(blockIdx.x, warp, a0, a1);
@@ -924,8 +897,8 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const __gr
     w[3] = static_cast<uint32_t>(b1);
     sw[warp] = StackWork{p.layers, p.L, w[0], w[1] - w[0], w[2], w[3] - w[2], p.gu.KT, p.dn.KT};
   }
-  // Down row tiles -> the CTAs holding them (one CTA: a whole-row word; several:
-  // the glue sums their partials), and each CTA's first row tile.
+  // Down row tiles -> the CTAs holding them (one CTA: `down` has the row;
+  // several: the glue sums their partials), and each CTA's first row tile.
   uint2* split = reinterpret_cast<uint2*>(smem + stack_tables_offset(p.nst, p.gu.KT, p.dn.KT, NC, p.H, p.ntok));
   uint32_t* span = reinterpret_cast<uint32_t*>(split + p.dn.RT);
   uint32_t* cfirst = span + p.dn.RT;
@@ -949,10 +922,30 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const __gr
     split[r] = o;
   }
   __syncthreads();
-  const unsigned long long seq = seq_s;
+  // TP: this CTA's whole down rows [prow0, prow1) (pushed to the peers), and
+  // the parity of layer 0's exchange slots.
+  uint32_t prow0 = 0, prow1 = 0, xpar0 = 0;
+  unsigned long long xbase = 0;
+  if (TP) {
+    const uint64_t c0 = ptB.cta_begin(blockIdx.x), c1 = ptB.cta_begin(blockIdx.x + 1);
+    prow0 = static_cast<uint32_t>((c0 + p.dn.KT - 1) / p.dn.KT);
+    prow1 = static_cast<uint32_t>(c1 / p.dn.KT);
+    if (prow1 < prow0) prow1 = prow0;
+    xbase = xbase_s;
+    xpar0 = static_cast<uint32_t>(xbase / p.world) & 1u;
+  }
   const uint32_t* my = wk[warp];
   ConsumerRing<kUnitsPerStage, StackWork> ring;
   ring.setup(smem, p.nst, warp, p.L * ((my[1] - my[0]) + (my[3] - my[2])), &sw[warp]);
+  // The previous layer's down projection as the glue reads it.
+  auto down_in = [&](uint32_t l) {
+    return DownIn{p.down, p.fxB.ws, split, cfirst, span, static_cast<uint32_t>(p.ntok) * 16,
+                  __ldg(&p.layers[l].dn_mul)};
+  };
+  auto down_in_x = [&](uint32_t l) {
+    return DownInX{xslot_ptr(p, p.rank, (xpar0 + l) & 1u, 0), p.xslot, p.world, p.xws_off, split, cfirst, span,
+                   static_cast<uint32_t>(p.ntok) * 16};
+  };
   // The act padding (k in [I, 64*dn.KT)) must read as zero in phase B.
   if (blockIdx.x == 0) {
     const uint32_t kpad = p.dn.KT * 64;
@@ -961,87 +954,69 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const __gr
       *reinterpret_cast<uint16_t*>(p.act + frag_offset(NC, n, k)) = 0;
     }
   }
-  constexpr uint32_t kTimeoutBit = TP ? kStatusPeerTimeout : kStatusGridTimeout;
-  uint8_t* xs = smem + base_smem_bytes(p.nst, p.ntok);
-  float* red = reinterpret_cast<float*>(xs + stack_xs_region(p.gu.KT, p.dn.KT, NC, p.H, p.ntok));
-  uint16_t* xres = reinterpret_cast<uint16_t*>(red + 32);  // the residual stream (bf16)
-  float* dsum = reinterpret_cast<float*>(xs + frag_bytes(p.gu.KT, NC));
-  // Partials of rows split between CTAs: scaled here (one rank: the sum of
-  // the partials times the scale, as the per-layer kernel's fix-up) or
-  // pre-scaled by each rank.
-  auto smul_of = [&](uint32_t l) { return TP ? 1.0f : __ldg(&p.layers[l].dn_mul); };
-  uint32_t barrier_epoch = 0;
 #pragma unroll 1
-  for (uint32_t l = 0; l < p.L; ++l) {
+  for (uint32_t i = 0; i < 2 * p.L; ++i) {
+    const uint32_t l = i >> 1;
+    const bool B = i & 1;
+    uint8_t* xs = smem + base_smem_bytes(p.nst, p.ntok);
     unsigned long long* tr = (l == 1) ? p.trace : nullptr;
-    trace_mark(tr, 0);
-    // ---- glue ----
-    const XnOut xn{nullptr, xs, static_cast<uint32_t>(NC), p.gu.KT * 64};
-    if (l == 0) {
-      glue<true, false>(p.ntok, p.H, p.eps, Bf16In{p.x_in}, NoIn{}, Bf16Out{xres}, xn, red);
-    } else {
-      const uint32_t pe = layer_epoch(seq, p.L, l - 1);
-      if (!ll_gather_any<TP>(p, (l - 1) & 1u, pe, smul_of(l - 1), split, cfirst, span, dsum, kTimeoutBit)) {
-        ring.drain();
-        return;
+    float* bdown = TP ? xslot_ptr(p, p.rank, (xpar0 + l) & 1u, p.rank) : p.down;
+    if (!B) {
+      float* red = reinterpret_cast<float*>(xs + stack_xs_region(p.gu.KT, p.dn.KT, NC, p.H, p.ntok));
+      uint16_t* xres = reinterpret_cast<uint16_t*>(red + 32);  // the residual stream (bf16)
+      trace_mark(tr, 0);
+      const XnOut xn{nullptr, xs, static_cast<uint32_t>(NC), p.gu.KT * 64};
+      if (l == 0) {
+        glue<true, false>(p.ntok, p.H, p.eps, Bf16In{p.x_in}, NoIn{}, Bf16Out{xres}, xn, red);
+      } else if constexpr (TP) {
+        glue<true, true>(p.ntok, p.H, p.eps, Bf16In{xres}, down_in_x(l - 1), Bf16Out{xres}, xn, red, tr);
+      } else {
+        glue<true, true>(p.ntok, p.H, p.eps, Bf16In{xres}, down_in(l - 1), Bf16Out{xres}, xn, red, tr);
       }
-      trace_mark(tr, 9);
-      glue<true, true>(p.ntok, p.H, p.eps, Bf16In{xres}, F32In{dsum}, Bf16Out{xres}, xn, red, tr);
+    } else {
+      stage_from_l2(xs, p.act, static_cast<uint32_t>(frag_bytes(p.dn.KT, NC)));
     }
     consumers_sync();
-    trace_mark(tr, 1);
-    // ---- phase A: gate/up -> act ----
-    {
-      const float sm = __ldg(&p.layers[l].gu_mul);
-      const StackEpi<TP> epi{false, p.act, &p, 0, 0, p.I, p.H, NC, sm, p.fn, 1.0f};
-      Fixup fx = p.fxA;
-      fx.part = reinterpret_cast<float*>(smem + ring_smem_bytes(p.nst));
-      const bool ok = consume_range<NC, false, FAST>(ring, p.gu, my[0], my[1], xs, fx, p.ntok, epi, p.status);
-      if (tr) {
-        consumers_sync();
-        trace_mark(tr, 7);
-      }
-      cta_fixup(ptA, &wk[0][0], fx, p.ntok, epi);
-      trace_mark(tr, 2);
-      const bool bar_ok = grid_barrier_epoch(p.bar, gridDim.x, bar_base, ++barrier_epoch, p.status);
-      if (!bar_ok || !consumers_and(ok)) {
-        ring.drain();
-        return;
-      }
-      trace_mark(tr, 3);
-    }
-    // ---- phase B: down -> LL words ----
-    {
-      stage_from_l2(xs, p.act, static_cast<uint32_t>(frag_bytes(p.dn.KT, NC)));
+    trace_mark(tr, B ? 4 : 1);
+    const float sm = B ? __ldg(&p.layers[l].dn_mul) : __ldg(&p.layers[l].gu_mul);
+    const StackEpi epi{B, p.act, bdown, p.I, p.H, NC, sm, p.fn, TP ? sm : 1.0f};
+    Fixup fx = B ? p.fxB : p.fxA;
+    if (TP && B) fx.ws = bdown + p.xws_off;
+    fx.part = reinterpret_cast<float*>(smem + ring_smem_bytes(p.nst));
+    const bool ok = consume_range<NC, false, FAST>(ring, B ? p.dn : p.gu, my[B ? 2 : 0], my[B ? 3 : 1], xs, fx,
+                                                   p.ntok, epi, p.status);
+    if (tr) {
       consumers_sync();
-      trace_mark(tr, 4);
-      const float sm = __ldg(&p.layers[l].dn_mul);
-      const StackEpi<TP> epi{true, p.act, &p, l & 1u, layer_epoch(seq, p.L, l), p.I, p.H, NC, sm, p.fn,
-                             TP ? sm : 1.0f};
-      Fixup fx{};
-      fx.part = reinterpret_cast<float*>(smem + ring_smem_bytes(p.nst));
-      const bool ok = consume_range<NC, false, FAST>(ring, p.dn, my[2], my[3], xs, fx, p.ntok, epi, p.status);
-      if (tr) {
-        consumers_sync();
-        trace_mark(tr, 8);
-      }
-      cta_fixup<true>(ptB, &wk[0][2], fx, p.ntok, epi);  // split rows: partials summed by the next glue
-      trace_mark(tr, 5);
-      if (!consumers_and(ok)) {
-        ring.drain();
-        return;
-      }
+      trace_mark(tr, B ? 8 : 7);
     }
+    if (B)
+      cta_fixup<true>(ptB, &wk[0][2], fx, p.ntok, epi);  // rows shared between CTAs: summed by the next glue
+    else
+      cta_fixup(ptA, &wk[0][0], fx, p.ntok, epi);
+    if (TP && B) push_down(p, (xpar0 + l) & 1u, prow0, prow1);
+    if (tr) {
+      consumers_sync();
+      trace_mark(tr, B ? 5 : 2);
+    }
+    bool bar_ok = grid_barrier_epoch(p.bar, gridDim.x, bar_base, i + 1, p.status);
+    if (TP && B && bar_ok) bar_ok = peer_exchange(p.xr, p.world, p.rank, xbase, l + 1, p.status);
+    if (!bar_ok || !consumers_and(ok)) {
+      ring.drain();
+      return;
+    }
+    trace_mark(tr, B ? 6 : 3);
   }
   if (blockIdx.x == 0) {
-    const uint32_t pe = layer_epoch(seq, p.L, p.L - 1);
-    if (!ll_gather_any<TP>(p, (p.L - 1) & 1u, pe, smul_of(p.L - 1), split, cfirst, span, dsum, kTimeoutBit)) return;
-    glue<false, true>(p.ntok, p.H, p.eps, Bf16In{xres}, F32In{dsum}, Bf16Out{p.out}, XnOut{}, red);
-    if (p.probe)
-      for (uint32_t e = threadIdx.x; e < static_cast<uint32_t>(p.ntok) * p.H; e += NTHR) p.probe[e] = dsum[e];
-    // Every CTA read the counter before its first layer and wrote its last
-    // layer's words before this glue could finish: advance it.
-    if (threadIdx.x == 0) asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(seq_ptr), "l"(seq + 1) : "memory");
+    float* red = reinterpret_cast<float*>(smem + base_smem_bytes(p.nst, p.ntok) +
+                                          stack_xs_region(p.gu.KT, p.dn.KT, NC, p.H, p.ntok));
+    const Bf16In xl{reinterpret_cast<uint16_t*>(red + 32)};
+    if constexpr (TP) {
+      glue<false, true>(p.ntok, p.H, p.eps, xl, down_in_x(p.L - 1), Bf16Out{p.out}, XnOut{}, red);
+      if (p.probe) write_probe(p.probe, p.ntok, p.H, down_in_x(p.L - 1));
+    } else {
+      glue<false, true>(p.ntok, p.H, p.eps, xl, down_in(p.L - 1), Bf16Out{p.out}, XnOut{}, red);
+      if (p.probe) write_probe(p.probe, p.ntok, p.H, down_in(p.L - 1));
+    }
   }
 }
 

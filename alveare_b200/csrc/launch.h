@@ -9,8 +9,10 @@
 namespace alv {
 
 // gemv_kernel with ready parameters (split: fp32 x as hi/lo columns;
-// ncols: fragment columns, a power of two).  Defined in gemv.cu.
-int launch_gemv_params(alv_ctx* ctx, const GemvParams& p, bool split, uint32_t ncols, cudaStream_t st);
+// ncols: fragment columns, a power of two; pdl: programmatic dependent
+// launch).  Defined in gemv.cu.
+int launch_gemv_params(alv_ctx* ctx, const GemvParams& p, bool split, uint32_t ncols, cudaStream_t st,
+                       bool pdl = false);
 
 // ffn_kernel with ready parameters (nt: tokens rounded up to a power of
 // two).  Defined in ffn.cu.

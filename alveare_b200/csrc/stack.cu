@@ -1,7 +1,6 @@
 // Host side of the C ABI, part 4: the one-launch FFN stack (ffn_stack_kernel)
 // and its tensor-parallel set-up over CUDA IPC.
-#include "internal.h"
-#include "kernels.cuh"
+#include "stack_launch.cuh"
 
 namespace alv {
 static_assert(kMaxRanksHost == kMaxRanks, "host and device agree on the rank limit");
@@ -9,72 +8,36 @@ static_assert(kMaxRanksHost == kMaxRanks, "host and device agree on the rank lim
 
 using namespace alv;
 
-// ===========================================================================
-// FFN stack: every layer of a decode step in one persistent launch
-// (ffn_stack_kernel).  The stack keeps its own workspace, so a launch
-// captured in a CUDA graph stays valid whatever else the context runs.
-// ===========================================================================
 namespace {
-constexpr int kStackMaxTokens = 4;
 
-// Exchange slot: [whole rows: kStackMaxTokens x H][CTA partials: #SMs x 2 x
-// kStackMaxTokens x 16], in 8-byte LL words, rows rounded up to 32 words.
-void exchange_shape(alv_ctx* ctx, const Weight* w, uint32_t* slot_words, uint32_t* rows_words) {
-  const size_t rows = (static_cast<size_t>(kStackMaxTokens) * w->H + 31) / 32 * 32;
-  const size_t parts = static_cast<size_t>(ctx->num_sms) * 2 * kStackMaxTokens * 16;
-  *rows_words = static_cast<uint32_t>(rows);
-  *slot_words = static_cast<uint32_t>((rows + parts + 31) / 32 * 32);
-}
-
-// Bytes of an exchange region: the header (launch counter) and 2 parities x
-// `world` slots.
-size_t region_bytes(const Weight* w, int world) {
-  return kXHeader + static_cast<size_t>(2) * world * w->xslot * 8;
-}
-
-// Stack workspace: [sync block: status @0, grid barrier @256, counters @1024]
-// [gate/up split-K partials][act][the one-rank exchange region].
 struct StackLayout {
-  size_t wsA, act, region, total;
+  size_t counters, wsA, wsB, down, act, total;
 };
 
 StackLayout stack_layout(alv_ctx* ctx, const Weight* w) {
   StackLayout o;
-  o.wsA = align_up(kHeaderBytes + static_cast<size_t>(w->a.m.RT + w->b.m.RT) * 4, 256);
-  o.act = align_up(o.wsA + ws_floats(ctx, kStackMaxTokens) * 4, 256);
-  o.region = align_up(o.act + frag_bytes(w->b.m.KT, kStackMaxTokens), 256);
-  o.total = align_up(o.region + region_bytes(w, 1), 256);
+  o.counters = kHeaderBytes;
+  o.wsA = align_up(o.counters + static_cast<size_t>(w->a.m.RT + w->b.m.RT) * 4, 256);
+  o.wsB = align_up(o.wsA + ws_floats(ctx, kStackMaxTokens) * 4, 256);
+  o.down = align_up(o.wsB + ws_floats(ctx, kStackMaxTokens) * 4, 256);
+  o.act = align_up(o.down + static_cast<size_t>(kStackMaxTokens) * w->H * 4, 256);
+  o.total = align_up(o.act + frag_bytes(w->b.m.KT, kStackMaxTokens), 256);
   return o;
 }
 
-template <int NT, bool FAST, bool TP>
-int launch_stack_t(alv_ctx* ctx, StackParams p, cudaStream_t st) {
-  const uint32_t nctas = static_cast<uint32_t>(ctx->num_sms);
-  const size_t other = stack_smem_bytes(0, p.gu.KT, p.dn.KT, NT, p.H, p.ntok, p.dn.RT, nctas);
-  p.nst = ring_stages(other);
-  if (!p.nst) return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn_stack: H, I or ntok too large for shared memory");
-  const size_t smem = stack_smem_bytes(p.nst, p.gu.KT, p.dn.KT, NT, p.H, p.ntok, p.dn.RT, nctas);
-  auto k = ffn_stack_kernel<NT, FAST, TP>;
-  // Grid barriers between the phases: every CTA must be resident at once.
-  int rc = prepare_kernel(ctx, k, smem, kThreadsPerCta, ctx->num_sms);
-  if (rc) return rc;
-  return launch_cooperative(ctx, k, p, ctx->num_sms, kThreadsPerCta, smem, st);
-}
-
-template <bool FAST, bool TP>
-int launch_stack_f(alv_ctx* ctx, const StackParams& p, uint32_t nt, cudaStream_t st) {
-  switch (nt) {
-    case 1: return launch_stack_t<1, FAST, TP>(ctx, p, st);
-    case 2: return launch_stack_t<2, FAST, TP>(ctx, p, st);
-    case 4: return launch_stack_t<4, FAST, TP>(ctx, p, st);
-  }
-  return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn_stack: unsupported token count");
+// Exchange slot of a tensor-parallel stack: [whole rows: kStackMaxTokens x H]
+// [CTA partials: #SMs x 2 x kStackMaxTokens x 16], in floats, 64-aligned.
+void exchange_shape(alv_ctx* ctx, const Weight* w, uint32_t* xslot, uint32_t* xws_off) {
+  const size_t rows = (static_cast<size_t>(kStackMaxTokens) * w->H + 63) / 64 * 64;
+  const size_t parts = static_cast<size_t>(ctx->num_sms) * 2 * kStackMaxTokens * 16;
+  *xws_off = static_cast<uint32_t>(rows);
+  *xslot = static_cast<uint32_t>((rows + parts + 63) / 64 * 64);
 }
 
 // Blob layout: [0, 64) cudaIpcMemHandle_t of the exchange region, [64, 80)
-// device UUID, [80, 100) u32 world, slot words, I-slice width, layers, SMs
-// (the ranks must agree on all five: they index each other's slots and
-// derive epochs from the same launch count and layer count).
+// device UUID, [80, 100) u32 world, slot floats, I-slice width, layers, SMs
+// (the ranks must agree on all five: each launch passes layers x world x SMs
+// peer-barrier arrivals).
 constexpr size_t kBlobUuid = 64, kBlobWorld = 80;
 static_assert(sizeof(cudaIpcMemHandle_t) <= kBlobUuid, "IPC handle larger than its blob field");
 }  // namespace
@@ -112,7 +75,6 @@ extern "C" int alv_ffn_stack_create(alv_ctx* ctx, const alv_handle* layers, int 
   s->i_end = w0->i_end;
   s->act = w0->act;
   s->layers.assign(layers, layers + n);
-  exchange_shape(ctx, s.get(), &s->xslot, &s->xws_off);
   const StackLayout lo = stack_layout(ctx, s.get());
   ALV_CUDA(ctx, dev_alloc(ctx, &s->layers_dev, sizeof(LayerW) * lw.size()));
   ALV_CUDA(ctx, cudaMemcpy(s->layers_dev, lw.data(), sizeof(LayerW) * lw.size(), cudaMemcpyHostToDevice));
@@ -156,25 +118,25 @@ extern "C" int alv_ffn_stack_run(alv_ctx* ctx, alv_handle h, int ntok, const uin
   p.eps = 1e-6f;
   p.x_in = x_in;
   p.out = out;
+  p.down = reinterpret_cast<float*>(w->ws + lo.down);
   p.act = w->ws + lo.act;
-  p.fxA = Fixup{reinterpret_cast<float*>(w->ws + lo.wsA), reinterpret_cast<uint32_t*>(w->ws + kHeaderBytes)};
+  uint32_t* cnt = reinterpret_cast<uint32_t*>(w->ws + lo.counters);
+  p.fxA = Fixup{reinterpret_cast<float*>(w->ws + lo.wsA), cnt};
+  p.fxB = Fixup{reinterpret_cast<float*>(w->ws + lo.wsB), cnt + w->a.m.RT};
   p.bar = reinterpret_cast<GridBar*>(w->ws + 256);
   p.status = reinterpret_cast<uint32_t*>(w->ws);
   p.trace = ctx->trace;
   p.probe = w->probe;
   const uint32_t nt = pow2_ceil(static_cast<uint32_t>(ntok));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  p.slot_words = w->xslot;
-  p.rows_words = w->xws_off;
   if (tp) {
     p.world = static_cast<uint32_t>(w->world);
     p.rank = static_cast<uint32_t>(w->rank);
     for (int q = 0; q < w->world; ++q) p.xr[q] = w->xr[q];
+    p.xslot = w->xslot;
+    p.xws_off = w->xws_off;
     return p.gu.fast ? launch_stack_f<true, true>(ctx, p, nt, st) : launch_stack_f<false, true>(ctx, p, nt, st);
   }
-  p.world = 1;
-  p.rank = 0;
-  p.xr[0] = w->ws + lo.region;
   return p.gu.fast ? launch_stack_f<true, false>(ctx, p, nt, st) : launch_stack_f<false, false>(ctx, p, nt, st);
 }
 
@@ -187,7 +149,8 @@ extern "C" int alv_ffn_stack_exchange(alv_ctx* ctx, alv_handle h, int world, voi
   if (w->xlocal) return fail(ctx, ALV_ERR_ARG, "ffn_stack_exchange: already called for this stack");
   int rc = set_device(ctx);
   if (rc) return rc;
-  const size_t bytes = region_bytes(w, world);
+  exchange_shape(ctx, w, &w->xslot, &w->xws_off);
+  const size_t bytes = kXHeader + static_cast<size_t>(2) * world * w->xslot * 4;
   ALV_CUDA(ctx, dev_alloc(ctx, &w->xlocal, bytes));
   ALV_CUDA(ctx, cudaMemset(w->xlocal, 0, bytes));
   ALV_CUDA(ctx, cudaDeviceSynchronize());
@@ -233,9 +196,7 @@ extern "C" int alv_ffn_stack_connect(alv_ctx* ctx, alv_handle h, int rank, int w
   }
   int rc = set_device(ctx);
   if (rc) return rc;
-  // Peers visible to this process must be reached over a link with native
-  // atomics (NVLink), which also keeps each aligned 64-bit store whole: the
-  // LL words of the exchange rely on that.
+  // Peers visible to this process must support native atomics over the link.
   int ndev = 0;
   ALV_CUDA(ctx, cudaGetDeviceCount(&ndev));
   for (int d = 0; d < ndev; ++d) {

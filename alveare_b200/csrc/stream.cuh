@@ -613,9 +613,9 @@ __device__ __forceinline__ void flush_tile(const float (&acc)[(NCOLS > 8 ? 2 : 1
 // ones inside the CTA's range.  Row tiles shared with other CTAs (unit-
 // balanced partitions only) get a CTA partial in fx.ws; unless DEFER, the
 // last CTA to arrive (acq_rel counter) sums them in CTA order and applies
-// epi.  With DEFER the partials go to epi.park(cta, slot, element, value)
-// and the consumer of the result sums them (the FFN stack's next glue).
-// All warps of the CTA call this (it syncs them).
+// epi.  With DEFER the partials are left for the consumer of the result to
+// sum after the next grid barrier (the FFN stack's next glue).  All warps of
+// the CTA call this (it syncs them).
 // ---------------------------------------------------------------------------
 template <bool DEFER = false, class Epi>
 __device__ void cta_fixup(const Partition& pt, const uint32_t* wr, const Fixup& fx, int ntok, const Epi& epi) {
@@ -636,7 +636,7 @@ __device__ void cta_fixup(const Partition& pt, const uint32_t* wr, const Fixup& 
     bool whole = false;
     for (uint32_t w = 0; w < kWarpsPerCtaS; ++w) {
       const uint32_t u0 = wr[4 * w], u1 = wr[4 * w + 1];
-      if (u0 < ie && u1 > ib) {
+      if (u0 < u1 && u0 < ie && u1 > ib) {  // a non-empty range that meets the tile
         w_lo = w < w_lo ? w : w_lo;
         w_hi = w;
         whole = u0 <= rb && u1 >= re;
@@ -650,15 +650,16 @@ __device__ void cta_fixup(const Partition& pt, const uint32_t* wr, const Fixup& 
       const int g = e & 7, tok = e >> 3;
       float vg = 0.f, vg8 = 0.f;
       for (uint32_t w = w_lo; w <= w_hi; ++w) {
+        if (!(wr[4 * w] < wr[4 * w + 1] && wr[4 * w] < ie && wr[4 * w + 1] > ib)) continue;  // an empty warp between contributors
         const float* src = fx.part + (static_cast<size_t>(w) * 2 + (r == wr[4 * w] / KT ? 0 : 1)) * slot_floats;
         vg += src[tok * 16 + g];
         vg8 += src[tok * 16 + g + 8];
       }
       if (inside) {
         epi.apply(r, g, tok, vg, vg8);
-      } else if constexpr (DEFER) {  // the epilogue stores (and may pre-scale) parked partials
-        epi.park(c, cslot, tok * 16 + g, vg);
-        epi.park(c, cslot, tok * 16 + g + 8, vg8);
+      } else if constexpr (DEFER) {  // the epilogue may pre-scale parked partials
+        cpart[tok * 16 + g] = epi.park(vg);
+        cpart[tok * 16 + g + 8] = epi.park(vg8);
       } else {
         cpart[tok * 16 + g] = vg;
         cpart[tok * 16 + g + 8] = vg8;

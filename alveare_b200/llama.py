@@ -162,6 +162,22 @@ class LlamaDecoder:
                                                      self._stream()), "alv_llama_tokens")
         return [int(t) for t in out]
 
+    def predicted(self, first: int, n: int) -> list[int]:
+        """Argmax predictions for positions [first, first + n) (teacher-forced
+        over a prompt, the greedy tokens past it)."""
+        out = np.empty(n, dtype=np.int32)
+        self.ctx.check(self.ctx.lib.alv_llama_predicted(self.ctx.ptr, self.handle, first, n, out.ctypes.data,
+                                                        self._stream()), "alv_llama_predicted")
+        return [int(t) for t in out]
+
+    def teacher_forced(self, sequence, n_context: int) -> list[int]:
+        """Feed `sequence` (context then continuation) and return the argmax
+        predicted at every continuation position: the model's next-token
+        choice given the true prefix, one greedy step per position."""
+        self.start(sequence)
+        self.run(n_context - 1, len(sequence) - n_context)
+        return self.predicted(n_context, len(sequence) - n_context)
+
     def free(self) -> None:
         if self.handle:
             self.ctx.lib.alv_weight_destroy(self.ctx.ptr, self.handle)

@@ -255,13 +255,20 @@ int alv_llama_load(alv_ctx* ctx, alv_handle model, const char* name, const void*
 int alv_llama_start(alv_ctx* ctx, alv_handle model, const int32_t* prompt, int n_prompt, void* stream);
 
 /* Enqueue n_prompt_steps steps without logits (prompt tokens), then
- * n_decode_steps greedy steps (LM head + argmax, the token written to the
- * next position).  Asynchronous, stream-ordered. */
+ * n_decode_steps steps with logits (LM head + argmax: the argmax becomes the
+ * next position's token unless the prompt already holds one there).
+ * Asynchronous, stream-ordered. */
 int alv_llama_run(alv_ctx* ctx, alv_handle model, int n_prompt_steps, int n_decode_steps, void* stream);
 
 /* Copy token ids [first, first + n) of the sequence to host memory
  * (synchronizes `stream`, reports device-side failures). */
 int alv_llama_tokens(alv_ctx* ctx, alv_handle model, int first, int n, int32_t* out_host, void* stream);
+
+/* The argmax each logits step computed for position p (p in [first,
+ * first + n)).  Past the prompt it equals the token at p; over a prompt it
+ * is a teacher-forced prediction (a prompt of a reference sequence scores
+ * every position of it in one run). */
+int alv_llama_predicted(alv_ctx* ctx, alv_handle model, int first, int n, int32_t* out_host, void* stream);
 
 /* start + run(n_prompt - 1, steps) + tokens(n_prompt, steps): the greedy loop
  * of tests/test_generation.py:72-99 without an EOS stop.  n_prompt + steps

@@ -9,8 +9,8 @@ each projection, norm, RoPE, attention and residual; fp32 inside), but fp32
 sums run in another order than numpy's, so an occasional bf16 rounding of a
 hidden state flips.  Logits are therefore held to a normwise bound per step
 (teacher-forced: both sides consume the same tokens), greedy tokens must
-match wherever the reference's top-two logits are apart, and the config-3
-run must reproduce the reference's tokens for at least the first 32 steps."""
+match wherever the reference's top-two logits are apart (bf16 logits tie
+exactly now and then, and a tie is decided by the last bit of an fp32 sum)."""
 import hashlib
 import json
 import os
@@ -87,12 +87,35 @@ def test_small_model_forward_and_generate_against_oracle():
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "llama_config3.json")
 
 
+def bf16_ulp(v: float) -> float:
+    return 2.0 ** (np.floor(np.log2(abs(v))) - 7)
+
+
+def near_tie(step: dict, ulps: float = 4.0) -> bool:
+    """The reference's greedy choice wins by at most `ulps` bf16 steps (0 is
+    an exact tie of bf16 logits, broken by the lower index)."""
+    return step["max"] - step["second"] <= ulps * bf16_ulp(step["max"])
+
+
 @pytest.mark.skipif(not os.path.exists(GOLDEN), reason="config-3 golden tokens not generated")
 def test_config3_greedy_tokens_match_reference():
     """Llama-3.2-1B shape, random-init Q4 (seed 0), a
     128-token random prompt and 256 greedy steps.  The weights are rebuilt
     here (the GPU quantizer is bit-exact with the reference's, checked by
-    the sha256 digests) and the GPU's tokens compared with the reference's."""
+    the sha256 digests) and the GPU's tokens compared with the reference's.
+
+    The logits are bf16, so the reference meets exact ties (step 11 of this
+    run: two tokens at 3.875, the lower index wins); there a one-ulp
+    difference in an fp32 sum decides, and no different-order fp32
+    arithmetic can promise the same pick.  The GPU's fp32 sums (tensor-core
+    accumulation, another order) differ from numpy's in the last bits, which
+    flips some of the ~700,000 bf16 roundings of a decode step; over 16
+    layers and the KV cache the bf16 logits drift by up to a few bf16 steps
+    (measured: up to 6 steps, most within 1).  So: free-running, the GPU must
+    follow the reference up to a step where the reference's top two logits
+    are within four bf16 steps; teacher-forced on the reference's sequence,
+    every step with a clear margin must pick the reference's token, and at
+    most 1 in 16 steps may differ."""
     gold = json.load(open(GOLDEN))
     cfg = llama.Config(max_seq=512)
     w, prompt = llama.synthetic_weights(cfg, seed=gold["seed"], quantize=gpu_quantize)
@@ -105,12 +128,17 @@ def test_config3_greedy_tokens_match_reference():
     assert hsh.hexdigest() == gold["weights_sha256"]["layers_packed"]
     dec = decoder_for(cfg, w)
     del w
-    steps = len(gold["tokens"])
+    ref = gold["tokens"]
+    steps = len(ref)
     got = dec.generate(gold["prompt"], steps)
-    agree = next((k for k, (a, b) in enumerate(zip(got, gold["tokens"])) if a != b), steps)
-    print(f"config 3: GPU greedy tokens agree with the reference for {agree} of {steps} steps")
+    agree = next((k for k, (a, b) in enumerate(zip(got, ref)) if a != b), steps)
+    print(f"config 3: free-running GPU greedy tokens equal the reference's for {agree} of {steps} steps")
     if agree < steps:
-        st = gold["steps"][agree]
-        print(f"first difference at step {agree}: reference top two {st['max']} / {st['second']}")
-    assert agree >= 32
+        assert near_tie(gold["steps"][agree]), gold["steps"][agree]
+    forced = dec.teacher_forced(gold["prompt"] + ref, len(gold["prompt"]))
+    miss = [k for k in range(steps) if forced[k] != ref[k]]
+    print(f"config 3: teacher-forced, {steps - len(miss)} of {steps} steps pick the reference's token; "
+          f"the others are near ties: {[(k, gold['steps'][k]['max'], gold['steps'][k]['second']) for k in miss]}")
+    assert all(near_tie(gold["steps"][k]) for k in miss)
+    assert len(miss) <= steps // 16
     dec.free()
