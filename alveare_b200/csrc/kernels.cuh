@@ -469,37 +469,6 @@ struct DownIn {
     return how == 0 ? a : (how == 1 ? (a + b) * sm : a * sm);
   }
 };
-// The down projection of a tensor-parallel layer: the sum over ranks, in
-// rank order, of each rank's DownIn (whole rows and CTA partials, all
-// pre-scaled) as the ranks pushed them into this GPU's exchange slots.
-// Every rank sums the same values in the same order, so every rank's
-// residual stream is identical.
-struct DownInX {
-  const float* slot0;       // this parity's slot of rank 0 (local memory)
-  uint32_t stride;          // floats from one rank's slot to the next
-  uint32_t world;
-  uint32_t ws_off;          // CTA partials within a slot
-  const uint2* split;
-  const uint32_t* cfirst;
-  const uint32_t* span;
-  uint32_t slot_floats;
-  __device__ __forceinline__ void load(uint32_t tok, uint32_t h, size_t i, float& a, float& b, uint32_t& how) const {
-    float v = 0.f;
-    for (uint32_t q = 0; q < world; ++q) {
-      const float* d = slot0 + static_cast<size_t>(q) * stride;
-      const DownIn di{d, d + ws_off, split, cfirst, span, slot_floats, 1.0f};
-      float x, y;
-      uint32_t hw;
-      di.load(tok, h, i, x, y, hw);
-      const float t = di.combine(x, y, hw);
-      v = q ? v + t : t;
-    }
-    a = v;
-    b = 0.f;
-    how = 0;
-  }
-  __device__ __forceinline__ float combine(float a, float, uint32_t) const { return a; }
-};
 struct NoIn {
   __device__ __forceinline__ void load(uint32_t, uint32_t, size_t, float& a, float& b, uint32_t& how) const {
     a = b = 0.f;
@@ -851,6 +820,63 @@ inline __device__ void push_down(const StackParams& p, uint32_t par, uint32_t ro
   }
 }
 
+// Tensor parallelism: sum the ranks' partial down projections of the
+// previous layer (their slots in this GPU's exchange region, complete after
+// the peer barrier) into dsum (fp32 [ntok][H], before the glue's bf16
+// rounding), every element as DownInX reads it -- each rank's whole-row value
+// or its CTA partials (pre-scaled) summed in CTA order, the ranks summed in
+// rank order -- but with element pairs loaded 8 bytes at a time and the
+// loads of up to four ranks in flight together (one element at a time would
+// wait one round trip per rank).
+static __device__ __noinline__ void tp_gather(const StackParams& p, uint32_t par, const uint2* split,
+                                       const uint32_t* cfirst, const uint32_t* span, float* dsum) {
+  constexpr uint32_t NTHR = kConsumerWarps * 32;
+  constexpr int WG = 4;                 // ranks per batch
+  const uint32_t H = p.H, ntok = static_cast<uint32_t>(p.ntok), W = p.world;
+  const uint32_t npairs = ntok * H / 2, sf = ntok * 16;
+  for (uint32_t pr = threadIdx.x; pr < npairs; pr += NTHR) {
+    const uint32_t e = 2 * pr, tok = e / H, h = e - tok * H, r = h >> 4;
+    const uint2 o = split[r];
+    const uint32_t el = tok * 16 + (h & 15);
+    float acc0 = 0.f, acc1 = 0.f;
+    for (uint32_t q0 = 0; q0 < W; q0 += WG) {
+      float2 a[WG], b[WG];
+#pragma unroll
+      for (int qq = 0; qq < WG; ++qq) {
+        a[qq] = b[qq] = make_float2(0.f, 0.f);
+        if (q0 + qq >= W) continue;
+        const float* d = xslot_ptr(p, p.rank, par, q0 + qq);
+        if (o.x == ~0u) {
+          a[qq] = __ldcg(reinterpret_cast<const float2*>(d + e));
+        } else if (o.y != ~0u) {
+          a[qq] = __ldcg(reinterpret_cast<const float2*>(d + p.xws_off + o.x + el));
+          b[qq] = __ldcg(reinterpret_cast<const float2*>(d + p.xws_off + o.y + el));
+        } else {  // a row tile over three or more CTAs (small problems)
+          const uint32_t sp = span[r];
+          for (uint32_t c = sp & 0xFFFFu; c <= (sp >> 16); ++c) {
+            const float2 v = __ldcg(reinterpret_cast<const float2*>(
+                d + p.xws_off + (static_cast<size_t>(c) * 2 + (r == cfirst[c] ? 0 : 1)) * sf + el));
+            a[qq].x += v.x;
+            a[qq].y += v.y;
+          }
+        }
+      }
+#pragma unroll
+      for (int qq = 0; qq < WG; ++qq) {
+        const uint32_t q = q0 + qq;
+        if (q >= W) continue;
+        const float t0 = o.x != ~0u && o.y != ~0u ? a[qq].x + b[qq].x : a[qq].x;
+        const float t1 = o.x != ~0u && o.y != ~0u ? a[qq].y + b[qq].y : a[qq].y;
+        acc0 = q ? acc0 + t0 : t0;
+        acc1 = q ? acc1 + t1 : t1;
+      }
+    }
+    dsum[e] = acc0;
+    dsum[e + 1] = acc1;
+  }
+  consumers_sync();
+}
+
 // The last layer's down projection as the final glue read it (fp32, summed
 // over CTAs and, with tensor parallelism, over ranks): a test probe.
 template <class DL>
@@ -942,10 +968,6 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const __gr
     return DownIn{p.down, p.fxB.ws, split, cfirst, span, static_cast<uint32_t>(p.ntok) * 16,
                   __ldg(&p.layers[l].dn_mul)};
   };
-  auto down_in_x = [&](uint32_t l) {
-    return DownInX{xslot_ptr(p, p.rank, (xpar0 + l) & 1u, 0), p.xslot, p.world, p.xws_off, split, cfirst, span,
-                   static_cast<uint32_t>(p.ntok) * 16};
-  };
   // The act padding (k in [I, 64*dn.KT)) must read as zero in phase B.
   if (blockIdx.x == 0) {
     const uint32_t kpad = p.dn.KT * 64;
@@ -969,7 +991,9 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const __gr
       if (l == 0) {
         glue<true, false>(p.ntok, p.H, p.eps, Bf16In{p.x_in}, NoIn{}, Bf16Out{xres}, xn, red);
       } else if constexpr (TP) {
-        glue<true, true>(p.ntok, p.H, p.eps, Bf16In{xres}, down_in_x(l - 1), Bf16Out{xres}, xn, red, tr);
+        float* dsum = reinterpret_cast<float*>(xs + frag_bytes(p.gu.KT, NC));  // after the x fragments
+        tp_gather(p, (xpar0 + l - 1) & 1u, split, cfirst, span, dsum);
+        glue<true, true>(p.ntok, p.H, p.eps, Bf16In{xres}, F32In{dsum}, Bf16Out{xres}, xn, red, tr);
       } else {
         glue<true, true>(p.ntok, p.H, p.eps, Bf16In{xres}, down_in(l - 1), Bf16Out{xres}, xn, red, tr);
       }
@@ -1011,8 +1035,11 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const __gr
                                           stack_xs_region(p.gu.KT, p.dn.KT, NC, p.H, p.ntok));
     const Bf16In xl{reinterpret_cast<uint16_t*>(red + 32)};
     if constexpr (TP) {
-      glue<false, true>(p.ntok, p.H, p.eps, xl, down_in_x(p.L - 1), Bf16Out{p.out}, XnOut{}, red);
-      if (p.probe) write_probe(p.probe, p.ntok, p.H, down_in_x(p.L - 1));
+      float* dsum = reinterpret_cast<float*>(smem + base_smem_bytes(p.nst, p.ntok) + frag_bytes(p.gu.KT, NC));
+      tp_gather(p, (xpar0 + p.L - 1) & 1u, split, cfirst, span, dsum);
+      glue<false, true>(p.ntok, p.H, p.eps, xl, F32In{dsum}, Bf16Out{p.out}, XnOut{}, red);
+      if (p.probe)
+        for (uint32_t e = threadIdx.x; e < static_cast<uint32_t>(p.ntok) * p.H; e += NTHR) p.probe[e] = dsum[e];
     } else {
       glue<false, true>(p.ntok, p.H, p.eps, xl, down_in(p.L - 1), Bf16Out{p.out}, XnOut{}, red);
       if (p.probe) write_probe(p.probe, p.ntok, p.H, down_in(p.L - 1));

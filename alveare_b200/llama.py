@@ -83,13 +83,19 @@ class LlamaDecoder:
     """Greedy Llama decode on one GPU (BASELINE config 3's model)."""
 
     def __init__(self, weights, config: LlamaConfig | None = None, device: int = 0, rope_theta: float = 500000.0):
+        if not isinstance(weights, dict):
+            cfg_path = os.path.join(str(weights), "config.json")
+            if os.path.exists(cfg_path):
+                c = json.load(open(cfg_path))
+                rope_theta = float(c.get("rope_theta", rope_theta))
+                if config is None and "hidden_size" in c:
+                    config = LlamaConfig(c["hidden_size"], c["intermediate_size"], c["num_attention_heads"],
+                                         c["num_key_value_heads"], c["head_dim"], c["num_hidden_layers"],
+                                         c["vocab_size"], 2048, 1e-5)
         self.cfg = config or LlamaConfig.llama32_1b()
         self.device = device
         self.ctx = _lib.context(device)
         if not isinstance(weights, dict):
-            cfg_path = os.path.join(str(weights), "config.json")
-            if os.path.exists(cfg_path):
-                rope_theta = float(json.load(open(cfg_path)).get("rope_theta", rope_theta))
             weights = load_weights_dir(weights, self.cfg.layers)
         h = ctypes.c_uint32()
         self.ctx.check(self.ctx.lib.alv_llama_create(self.ctx.ptr, ctypes.byref(self.cfg), ctypes.byref(h)),

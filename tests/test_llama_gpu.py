@@ -142,3 +142,36 @@ def test_config3_greedy_tokens_match_reference():
     assert all(near_tie(gold["steps"][k]) for k in miss)
     assert len(miss) <= steps // 16
     dec.free()
+
+
+def test_quantized_directory_round_trip(tmp_path):
+    """Float weights -> the reference's quantized-model directory on the GPU
+    (alveare_b200.quantize, tools/quantize_model.py) -> LlamaDecoder(dir):
+    the same greedy tokens as the oracle reading that directory."""
+    from alveare_b200.llama import load_weights_dir
+    from alveare_b200.quantize import quantize_llama
+    rng = np.random.default_rng(5)
+    H, I, V, heads, kv, L = 256, 512, 1000, 4, 2, 2
+    hd = H // heads
+    t = {"token_embd.weight": rng.normal(0, 0.02, (V, H)).astype(np.float32), "output_norm.weight": np.ones(H, np.float32)}
+    shapes = {"attn_q": (H, H), "attn_k": (kv * hd, H), "attn_v": (kv * hd, H), "attn_output": (H, H),
+              "ffn_gate": (I, H), "ffn_up": (I, H), "ffn_down": (H, I)}
+    for l in range(L):
+        t[f"blk.{l}.attn_norm.weight"] = np.ones(H, np.float32)
+        t[f"blk.{l}.ffn_norm.weight"] = np.ones(H, np.float32)
+        for p, s in shapes.items():
+            t[f"blk.{l}.{p}.weight"] = rng.normal(0, 0.02, s).astype(np.float32)
+    quantize_llama(t, tmp_path, heads=heads, kv_heads=kv)
+    w = load_weights_dir(tmp_path, L)
+    assert np.array_equal(w["blk.1.ffn_up.weight_packed"], q4.quantize_combined(t["blk.1.ffn_up.weight"]))
+    cfg = llama.Config(hidden=H, intermediate=I, heads=heads, kv_heads=kv, head_dim=hd, layers=L, vocab=V,
+                       vocab_padded=2048, max_seq=2048)
+    orc = llama.LlamaOracle(cfg, {k: np.asarray(v) for k, v in w.items()})
+    prompt = [1, 2, 3, 500, 999]
+    ref = orc.generate(prompt, 6)
+    dec = LlamaDecoder(str(tmp_path))
+    assert dec.cfg.hidden == H and dec.cfg.layers == L
+    got = dec.generate(prompt, 6)
+    agree = next((k for k, (a, b) in enumerate(zip(got, ref)) if a != b), len(got))
+    assert agree >= 4, (got, ref)
+    dec.free()
