@@ -412,9 +412,30 @@ constexpr int kGlueRegs = 16;
 constexpr int kMaxRanks = 8;  // tensor-parallel ranks of one FFN stack
 
 // Loaders: value of token tok at index h, flat index i = tok * H + h.
+// 8 consecutive values at flat index i (a multiple of 8): one 16-byte access
+// when the address allows it (shared or global memory alike).
+__device__ __forceinline__ bool al16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; }
+__device__ __forceinline__ void unpack8(const uint4& w, float (&v)[8]) {
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    v[2 * t] = bf16_bits_to_f32(ws[t] & 0xFFFFu);
+    v[2 * t + 1] = bf16_bits_to_f32(ws[t] >> 16);
+  }
+}
+
 struct Bf16In {   // bf16 values in memory written before the launch (or shared)
   const uint16_t* p;
   __device__ __forceinline__ float operator()(uint32_t, uint32_t, size_t i) const { return bf16_bits_to_f32(p[i]); }
+  __device__ __forceinline__ void load8(size_t i, float (&v)[8]) const {
+    const uint16_t* q = p + i;
+    if (al16(q)) {
+      unpack8(*reinterpret_cast<const uint4*>(q), v);
+    } else {
+#pragma unroll
+      for (int t = 0; t < 8; ++t) v[t] = bf16_bits_to_f32(q[t]);
+    }
+  }
 };
 struct F32In {    // fp32 values in memory written before the launch (or shared)
   const float* p;
@@ -425,6 +446,16 @@ struct F32In {    // fp32 values in memory written before the launch (or shared)
     how = 0;
   }
   __device__ __forceinline__ float combine(float a, float, uint32_t) const { return a; }
+  __device__ __forceinline__ void load8(uint32_t, uint32_t, size_t i, float (&v)[8]) const {
+    const float* q = p + i;
+    if (al16(q)) {
+      const float4 a = *reinterpret_cast<const float4*>(q), b = *reinterpret_cast<const float4*>(q + 4);
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+#pragma unroll
+      for (int t = 0; t < 8; ++t) v[t] = q[t];
+    }
+  }
 };
 // The down projection of the previous stack layer as the glue reads it
 // (token tok, index h, flat i = tok*H + h): a row tile held by one CTA is
@@ -468,6 +499,38 @@ struct DownIn {
   __device__ __forceinline__ float combine(float a, float b, uint32_t how) const {
     return how == 0 ? a : (how == 1 ? (a + b) * sm : a * sm);
   }
+  // Elements h..h+7 (h a multiple of 8: one row tile, one half of it),
+  // combined as above.
+  __device__ __forceinline__ void load8(uint32_t tok, uint32_t h, size_t i, float (&v)[8]) const {
+    const uint32_t r = h >> 4;
+    const uint2 o = split[r];
+    const uint32_t e = tok * 16 + (h & 15);
+    auto ld8 = [](const float* q, float (&w)[8]) {
+      const float4 a = __ldcg(reinterpret_cast<const float4*>(q)), b = __ldcg(reinterpret_cast<const float4*>(q + 4));
+      w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w; w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+    };
+    if (o.x == ~0u) {
+      ld8(down + i, v);
+    } else if (o.y != ~0u) {
+      float a[8], b[8];
+      ld8(ws + o.x + e, a);
+      ld8(ws + o.y + e, b);
+#pragma unroll
+      for (int t = 0; t < 8; ++t) v[t] = (a[t] + b[t]) * sm;
+    } else {  // a row tile over three or more CTAs (small problems)
+      const uint32_t sp = span[r];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) v[t] = 0.f;
+      for (uint32_t c = sp & 0xFFFFu; c <= (sp >> 16); ++c) {
+        float a[8];
+        ld8(ws + (static_cast<size_t>(c) * 2 + (r == cfirst[c] ? 0 : 1)) * slot_floats + e, a);
+#pragma unroll
+        for (int t = 0; t < 8; ++t) v[t] += a[t];
+      }
+#pragma unroll
+      for (int t = 0; t < 8; ++t) v[t] *= sm;
+    }
+  }
 };
 struct NoIn {
   __device__ __forceinline__ void load(uint32_t, uint32_t, size_t, float& a, float& b, uint32_t& how) const {
@@ -475,11 +538,30 @@ struct NoIn {
     how = 0;
   }
   __device__ __forceinline__ float combine(float a, float, uint32_t) const { return a; }
+  __device__ __forceinline__ void load8(uint32_t, uint32_t, size_t, float (&v)[8]) const {
+#pragma unroll
+    for (int t = 0; t < 8; ++t) v[t] = 0.f;
+  }
 };
 struct Bf16Out {  // null: no output
   uint16_t* p;
   __device__ __forceinline__ void operator()(size_t i, float v) const {
     if (p) p[i] = bf16_bits_rn(v);
+  }
+  __device__ __forceinline__ void store8(size_t i, const float (&v)[8]) const {
+    if (!p) return;
+    uint16_t* q = p + i;
+    if (al16(q)) {
+      uint4 w;
+      w.x = pack_bf2(bf16_bits_rn(v[0]), bf16_bits_rn(v[1]));
+      w.y = pack_bf2(bf16_bits_rn(v[2]), bf16_bits_rn(v[3]));
+      w.z = pack_bf2(bf16_bits_rn(v[4]), bf16_bits_rn(v[5]));
+      w.w = pack_bf2(bf16_bits_rn(v[6]), bf16_bits_rn(v[7]));
+      *reinterpret_cast<uint4*>(q) = w;
+    } else {
+#pragma unroll
+      for (int t = 0; t < 8; ++t) q[t] = bf16_bits_rn(v[t]);
+    }
   }
 };
 
@@ -503,65 +585,82 @@ __device__ __forceinline__ void stage_from_l2(uint8_t* dst, const uint8_t* src, 
     *reinterpret_cast<uint4*>(dst + o) = __ldcg(reinterpret_cast<const uint4*>(src + o));
 }
 
-template <int GR, bool PRE, bool HAS_D, class XL, class DL, class XO>
+template <int GK, bool PRE, bool HAS_D, class XL, class DL, class XO>
 __device__ void glue_tokens(int ntok, uint32_t H, float eps, const XL& xl, const DL& dl, const XO& xo,
                             const XnOut& xn_out, float* red, unsigned long long* tr) {
   constexpr uint32_t NTHR = kConsumerWarps * 32;
   static_assert(kConsumerWarps <= 16, "consumers_sum buffers hold 16 partials");
   const float hf = static_cast<float>(H);
+  const uint32_t G = H / 8;  // groups of 8 consecutive values; thread t owns groups t + k * NTHR
   // consumers_sum alternates between red[0..15] and red[16..31]; the caller's
   // barrier before the glue orders this glue's first use after the last one
   // of the previous glue.
   int rs = 0;
   for (int tok = 0; tok < ntok; ++tok) {
     const size_t base = static_cast<size_t>(tok) * H;
-    // Two passes so every load of the token is in flight before any is used.
-    float xv[GR], dv[GR], db[GR];
-    uint32_t how = 0;  // 2 bits per element
+    // All loads of the token in flight before any is used.
+    float xv[GK][8], dv[GK][8];
 #pragma unroll
-    for (int i = 0; i < GR; ++i) {
-      const uint32_t h = threadIdx.x + i * NTHR;
-      xv[i] = h < H ? xl(tok, h, base + h) : 0.f;
-      dv[i] = db[i] = 0.f;
-      uint32_t hw = 0;
-      if (HAS_D && h < H) dl.load(tok, h, base + h, dv[i], db[i], hw);
-      how |= hw << (2 * i);
+    for (int k = 0; k < GK; ++k) {
+      const uint32_t g = threadIdx.x + k * NTHR;
+#pragma unroll
+      for (int t = 0; t < 8; ++t) xv[k][t] = dv[k][t] = 0.f;
+      if (g < G) {
+        xl.load8(base + 8 * g, xv[k]);
+        if (HAS_D) dl.load8(static_cast<uint32_t>(tok), 8 * g, base + 8 * g, dv[k]);
+      }
     }
-#pragma unroll
-    for (int i = 0; i < GR; ++i) dv[i] = HAS_D ? bf16_round(dl.combine(dv[i], db[i], (how >> (2 * i)) & 3)) : 0.f;
     if (tok == 0) trace_mark(tr, 9);
     if (HAS_D) {
       float ss = 0.f;
 #pragma unroll
-      for (int i = 0; i < GR; ++i) ss = fmaf(dv[i], dv[i], ss);
+      for (int k = 0; k < GK; ++k)
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          dv[k][t] = bf16_round(dv[k][t]);
+          ss = fmaf(dv[k][t], dv[k][t], ss);
+        }
       ss = consumers_sum(ss, red + 16 * (rs++ & 1));
       if (tok == 0) trace_mark(tr, 10);
       const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, hf), eps)));
 #pragma unroll
-      for (int i = 0; i < GR; ++i) xv[i] = bf16_round(xv[i] + bf16_round(dv[i] * inv));
+      for (int k = 0; k < GK; ++k)
+#pragma unroll
+        for (int t = 0; t < 8; ++t) xv[k][t] = bf16_round(xv[k][t] + bf16_round(dv[k][t] * inv));
     }
 #pragma unroll
-    for (int i = 0; i < GR; ++i) {
-      const uint32_t h = threadIdx.x + i * NTHR;
-      if (h < H) xo(base + h, xv[i]);
+    for (int k = 0; k < GK; ++k) {
+      const uint32_t g = threadIdx.x + k * NTHR;
+      if (g < G) xo.store8(base + 8 * g, xv[k]);
     }
     if (PRE) {
       float ss = 0.f;
 #pragma unroll
-      for (int i = 0; i < GR; ++i) ss = fmaf(xv[i], xv[i], ss);
+      for (int k = 0; k < GK; ++k)
+#pragma unroll
+        for (int t = 0; t < 8; ++t) ss = fmaf(xv[k][t], xv[k][t], ss);
       ss = consumers_sum(ss, red + 16 * (rs++ & 1));
       if (tok == 0) trace_mark(tr, 11);
       const float inv = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, hf), eps)));
 #pragma unroll
-      for (int i = 0; i < GR; ++i) {
-        const uint32_t h = threadIdx.x + i * NTHR;
-        if (h >= H) continue;
-        const float xn = bf16_round(xv[i] * inv);
-        if (xn_out.frag)
-          *reinterpret_cast<uint16_t*>(xn_out.frag + frag_offset(xn_out.nc, static_cast<uint32_t>(tok), h)) =
-              bf16_bits_rn(xn);
-        else
-          xn_out.tmp[base + h] = xn;
+      for (int k = 0; k < GK; ++k) {
+        const uint32_t g = threadIdx.x + k * NTHR;
+        if (g >= G) continue;
+        const uint32_t h = 8 * g;
+        float xn[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) xn[t] = bf16_round(xv[k][t] * inv);
+        if (xn_out.frag) {
+          // values h + 2i, h + 2i + 1 share one 32-bit word; the four words
+          // of a group sit 32 bytes apart (fragment lane quads t4 = i)
+          uint8_t* f = xn_out.frag + frag_offset(xn_out.nc, static_cast<uint32_t>(tok), h);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            *reinterpret_cast<uint32_t*>(f + 32 * i) = pack_bf2(bf16_bits_rn(xn[2 * i]), bf16_bits_rn(xn[2 * i + 1]));
+        } else {
+#pragma unroll
+          for (int t = 0; t < 8; ++t) xn_out.tmp[base + h + t] = xn[t];
+        }
       }
     }
   }
@@ -581,16 +680,16 @@ __device__ void glue_tokens(int ntok, uint32_t H, float eps, const XL& xl, const
   consumers_sync();
 }
 
-// GR chosen from H at run time (8 covers H <= 3840).
+// Groups of 8 per thread chosen from H at run time (one covers H <= 3840).
 // tr: optional phase stamps [9] down loaded, [10] its norm reduced, [11] x's
 // norm reduced, [12] xn written (first token).
 template <bool PRE, bool HAS_D, class XL, class DL, class XO>
 __device__ __forceinline__ void glue(int ntok, uint32_t H, float eps, const XL& xl, const DL& dl, const XO& xo,
                                      const XnOut& xn_out, float* red, unsigned long long* tr = nullptr) {
   if (H <= 8u * kConsumerWarps * 32)
-    glue_tokens<8, PRE, HAS_D>(ntok, H, eps, xl, dl, xo, xn_out, red, tr);
+    glue_tokens<1, PRE, HAS_D>(ntok, H, eps, xl, dl, xo, xn_out, red, tr);
   else
-    glue_tokens<kGlueRegs, PRE, HAS_D>(ntok, H, eps, xl, dl, xo, xn_out, red, tr);
+    glue_tokens<kGlueRegs / 8, PRE, HAS_D>(ntok, H, eps, xl, dl, xo, xn_out, red, tr);
 }
 
 template <int NT, bool SPLIT, bool FAST>
