@@ -81,7 +81,10 @@ int do_gemv(alv_ctx* ctx, Weight* w, int ntok, const void* x, int x_dtype, void*
   GemvParams p = gemv_params(w, ntok, x, x_dtype, y, y_dtype);
   p.fx = Fixup{reinterpret_cast<float*>(work_ptr(ctx)), counters_ptr(ctx)};
   p.status = status_ptr(ctx);
-  return launch_gemv_params(ctx, p, x_dtype == ALV_F32, ncols, st);
+  // Programmatic dependent launch: the kernel streams its weights while the
+  // previous kernel in the stream finishes, and reads x / writes y only after
+  // griddepcontrol.wait.
+  return launch_gemv_params(ctx, p, x_dtype == ALV_F32, ncols, st, true);
 }
 
 }  // namespace alv

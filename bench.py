@@ -338,8 +338,74 @@ def extra_configs(device: int) -> dict:
     out["decode_batch_sweep_15360x3840"] = sweep
     for w in ws:
         w.free()
+    del ws
     torch.cuda.synchronize(dev)
+    out["config3_llama32_1b_greedy_decode"] = llama_decode(device)
     return out
+
+
+def llama_decode(device: int, steps: int = 256, n_prompt: int = 128) -> dict:
+    """Llama-3.2-1B shape, random-init Q4 weights (N(0,
+    0.02), quantized on the GPU; K/V padding rows zero as on disk), a
+    128-token random prompt, then `steps` greedy tokens; tokens/s of the
+    device-side greedy loop (one CUDA graph per step) and the Q4 bytes a
+    token streams."""
+    import torch
+
+    from alveare_b200.llama import LlamaConfig, LlamaDecoder
+    dev = torch.device("cuda", device)
+    cfg = LlamaConfig.llama32_1b(max_seq=n_prompt + steps)
+    H, Iw, V = cfg.hidden, cfg.intermediate, cfg.vocab
+    kv = cfg.kv_heads * cfg.head_dim
+    Vp = (V + 2047) // 2048 * 2048
+    g = torch.Generator(device=dev)
+    g.manual_seed(77)
+    emb = torch.randn((V, H), generator=g, device=dev).mul_(0.02).half()
+    lm = torch.zeros((Vp, H), device=dev)
+    lm[:V] = emb.float()
+    w = {"token_embd": emb, "output_norm.weight": torch.ones(H, device=dev), "lm_head_packed": q4_quantize_dev(lm)}
+    del lm
+    shapes = {"attn_q": (H, H, H), "attn_k": (H, H, kv), "attn_v": (H, H, kv), "attn_output": (H, H, H),
+              "ffn_gate": (Iw, H, Iw), "ffn_up": (Iw, H, Iw), "ffn_down": (H, Iw, H)}
+    weight_bytes = Vp * H // 32 * 18
+    for l in range(cfg.layers):
+        w[f"blk.{l}.attn_norm.weight"] = torch.ones(H, device=dev)
+        w[f"blk.{l}.ffn_norm.weight"] = torch.ones(H, device=dev)
+        for p, (rows, cols, real) in shapes.items():
+            m = torch.zeros((rows, cols), device=dev)
+            m[:real] = torch.randn((real, cols), generator=g, device=dev).mul_(0.02)
+            w[f"blk.{l}.{p}.weight_packed"] = q4_quantize_dev(m)
+            weight_bytes += real * cols // 32 * 18   # the padding rows are not streamed
+            del m
+    dec = LlamaDecoder(w, cfg, device=device)
+    del w
+    prompt = torch.randint(0, V, (n_prompt,), generator=torch.Generator().manual_seed(78)).tolist()
+    st = torch.cuda.current_stream(dev)
+    for _ in range(2):   # warm-up (graph capture on the first)
+        dec.start(prompt)
+        dec.run(n_prompt - 1, 8)
+    dec.start(prompt)
+    dec.run(n_prompt - 1, 0)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st.synchronize()
+    e0.record(st)
+    dec.run(0, steps)
+    e1.record(st)
+    st.synchronize()
+    ms = e0.elapsed_time(e1)
+    toks = dec.tokens(n_prompt, steps)
+    dec.free()
+    us = ms * 1e3 / steps
+    return {"us_per_token": round(us, 2), "tokens_per_s": round(steps / ms * 1e3, 1),
+            "q4_bytes_per_token": weight_bytes, "gbs": round(weight_bytes / us / 1e3, 1),
+            "frac_of_hbm": round(weight_bytes / us / 1e3 / load_peaks()["hbm_gbs"], 4),
+            "steps": steps, "prompt": n_prompt, "distinct_tokens": len(set(toks)),
+            "l2": "695 MB of weights per token vs 126 MB L2"}
+
+
+def q4_quantize_dev(w):
+    from alveare_b200 import q4_quantize
+    return q4_quantize(w)
 
 
 def load_peaks_tc() -> float:
