@@ -15,6 +15,11 @@ int launch_ffn_t(alv_ctx* ctx, FfnParams p, cudaStream_t st) {
     if (p.glue_tma) other += v * 2 + (p.down_in ? v * 4 : 0);    // raw inputs
   }
   other += 16;                                                   // input mbarrier
+  const uint32_t nctas = static_cast<uint32_t>(ctx->num_sms);
+  if (!Partition::fits(p.gu.RT, p.gu.KT) || !Partition::fits(p.dn.RT, p.dn.KT))
+    return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn: matrix too large for one launch's partition");
+  p.ptA = Partition::make(p.gu.RT, p.gu.KT, nctas, true);
+  p.ptB = Partition::make(p.dn.RT, p.dn.KT, nctas);
   p.nst = ring_stages(other);
   if (!p.nst) return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn: H or I too large for the shared-memory fragment stage");
   const size_t smem = ring_smem_bytes(p.nst) + other;

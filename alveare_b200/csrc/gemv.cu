@@ -5,11 +5,24 @@
 namespace alv {
 namespace {
 
+// Ring stages a gemv CTA requests before it stages x.  Its x loads queue
+// behind every byte already requested from HBM, so all stages up front
+// (about the whole matrix for decode shapes) make x arrive late and stall
+// the stream; one stage per warp keeps HBM busy while x is fetched.
+constexpr uint32_t kGemvFirstStages = 1;
+
 template <int NCOLS, bool SPLIT, bool FAST>
 int launch_gemv_t(alv_ctx* ctx, GemvParams p, cudaStream_t st, bool pdl) {
   const size_t other = part_bytes(p.x.ntok) + frag_bytes(p.m.KT, NCOLS);
   p.nst = ring_stages(other);
   if (!p.nst) return fail(ctx, ALV_ERR_UNSUPPORTED, "gemv: K too large for the shared-memory fragment stage");
+  p.first = kGemvFirstStages;
+  // Row-aligned unless there are too few row tiles to keep the SMs busy: a
+  // row tile split between CTAs costs the finishing CTA a fence, an atomic
+  // and a round trip at the end, more than the imbalance of whole rows.
+  const uint32_t nctas = static_cast<uint32_t>(ctx->num_sms);
+  if (!Partition::fits(p.m.RT, p.m.KT)) return fail(ctx, ALV_ERR_UNSUPPORTED, "gemv: matrix too large for one launch");
+  p.pt = Partition::make(p.m.RT, p.m.KT, nctas, p.m.RT * 4 >= nctas);
   const size_t smem = ring_smem_bytes(p.nst) + other;
   auto k = gemv_kernel<NCOLS, SPLIT, FAST>;
   // gemv_kernel has no grid barrier (split rows are finished by the last CTA
@@ -81,6 +94,7 @@ int do_gemv(alv_ctx* ctx, Weight* w, int ntok, const void* x, int x_dtype, void*
   GemvParams p = gemv_params(w, ntok, x, x_dtype, y, y_dtype);
   p.fx = Fixup{reinterpret_cast<float*>(work_ptr(ctx)), counters_ptr(ctx)};
   p.status = status_ptr(ctx);
+  p.trace = ctx->trace;
   // Programmatic dependent launch: the kernel streams its weights while the
   // previous kernel in the stream finishes, and reads x / writes y only after
   // griddepcontrol.wait.

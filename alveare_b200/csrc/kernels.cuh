@@ -161,6 +161,17 @@ struct GridBar {
   unsigned long long count;  // monotonically increasing arrivals (never wraps)
 };
 
+// floor(n / d) for a counter n < 2^50 and d >= 1: a double-precision
+// estimate (relative error below 2^-51, so within one of the quotient)
+// corrected with integer products -- a few instructions where a 64-bit
+// integer division is a long software sequence on the barrier's critical path.
+__device__ __forceinline__ unsigned long long div_counter(unsigned long long n, uint32_t d) {
+  unsigned long long q = static_cast<unsigned long long>(__dmul_rn(static_cast<double>(n), __drcp_rn(static_cast<double>(d))));
+  if (q * d > n) --q;
+  if ((q + 1) * d <= n) ++q;
+  return q;
+}
+
 // One atomic per CTA: the k-th use of the barrier completes when the counter
 // reaches k * nblocks; waiters poll the counter itself.  Correct across
 // launches because every launch uses it a whole number of times with the
@@ -171,7 +182,7 @@ inline __device__ bool grid_barrier(GridBar* gb, uint32_t nblocks, uint32_t* sta
   if (threadIdx.x == 0) {
     __threadfence();
     const unsigned long long arrived = atomicAdd(&gb->count, 1ull);
-    const unsigned long long target = (arrived / nblocks + 1) * nblocks;
+    const unsigned long long target = (div_counter(arrived, nblocks) + 1) * nblocks;
     volatile unsigned long long* vc = &gb->count;
     if (*vc < target) {
       const unsigned long long t0 = globaltimer_ns();
@@ -198,7 +209,7 @@ __device__ __forceinline__ unsigned long long grid_base(GridBar* gb, uint32_t nb
   // first barrier needs every CTA), and launches start at multiples of nblocks.
   unsigned long long v;
   asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(&gb->count) : "memory");
-  return v / nblocks * nblocks;
+  return div_counter(v, nblocks) * nblocks;
 }
 inline __device__ bool grid_barrier_epoch(GridBar* gb, uint32_t nblocks, unsigned long long base, uint32_t epoch,
                                    uint32_t* status) {
@@ -238,7 +249,7 @@ inline __device__ bool grid_barrier_epoch(GridBar* gb, uint32_t nblocks, unsigne
 __device__ __forceinline__ unsigned long long peer_base(const uint8_t* own, uint32_t world) {
   unsigned long long v;
   asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(own) : "memory");
-  return v / world * world;
+  return div_counter(v, world) * world;
 }
 inline __device__ bool peer_exchange(uint8_t* const* xr, uint32_t world, uint32_t rank, unsigned long long base,
                               uint32_t epoch, uint32_t* status) {
@@ -306,11 +317,14 @@ inline __device__ float block_sum(float v, float* red) {
 // ===========================================================================
 struct GemvParams {
   Q4Mat m;
+  Partition pt;  // the launch's split of m's units (host-built for the grid)
   XSrc x;
   RowsEpi epi;
   Fixup fx;
   uint32_t* status;
-  uint32_t nst;  // ring stages per warp
+  uint32_t nst;    // ring stages per warp
+  uint32_t first;  // stages requested before x is staged (the rest after)
+  unsigned long long* trace;  // optional: [gridDim.x][16] phase timestamps (ns)
 };
 
 constexpr int kUnitsPerStage = ALV_UNITS_PER_STAGE;
@@ -327,39 +341,49 @@ __host__ __device__ constexpr size_t base_smem_bytes(uint32_t nst, int ntok) {
   return ring_smem_bytes(nst) + part_bytes(ntok);
 }
 
+// Phase timestamps of one gemv CTA (thread 0): 0 start, 1 weights requested,
+// 2 predecessor finished (griddepcontrol.wait returned), 3 x staged, 4 warp
+// 0's units consumed, 5 split-K reduction done.
+__device__ __forceinline__ void gemv_mark(unsigned long long* trace, int i) {
+  if (trace && threadIdx.x == 0) trace[blockIdx.x * 16 + i] = globaltimer_ns();
+}
+
 template <int NCOLS, bool SPLIT, bool FAST>
 __global__ void __launch_bounds__(kThreadsPerCta, 1) gemv_kernel(const GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ WorkList wl[kConsumerWarps];
   __shared__ uint32_t wr[kConsumerWarps][4];  // per warp: unit range [u0, u1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Row-aligned unless there are too few row tiles to keep the SMs busy: a
-  // row tile split between CTAs costs the finishing CTA a fence, an atomic
-  // and a round trip at the end, more than the imbalance of whole rows.
-  const Partition pt = Partition::make(p.m.RT, p.m.KT, gridDim.x, p.m.RT * 4 >= gridDim.x);
+  const Partition& pt = p.pt;
+  gemv_mark(p.trace, 0);
   Shape::init_barriers(smem, p.nst);
-  uint64_t w0, w1;
-  pt.warp_range(blockIdx.x, warp, w0, w1);
-  const uint32_t u0 = static_cast<uint32_t>(w0), u1 = static_cast<uint32_t>(w1);
+  uint32_t u0, u1;
+  pt.warp_range(blockIdx.x, warp, u0, u1);
   if (lane == 0) {
     wl[warp] = WorkList{p.m.units + static_cast<size_t>(u0) * kUnitBytes, p.m.units, u1 - u0, 0,
-                        u0 % p.m.KT, 0, p.m.KT, 1};
+                        u0 - pt.kt.div(u0) * p.m.KT, 0, p.m.KT, 1};
     wr[warp][0] = u0;
     wr[warp][1] = u1;
   }
   __syncthreads();
   pdl_trigger();
   ConsumerRing<kUnitsPerStage, WorkList> ring;
-  ring.setup(smem, p.nst, warp, u1 - u0, &wl[warp]);  // weights start streaming
+  ring.setup(smem, p.nst, warp, u1 - u0, &wl[warp], p.first);  // weights start streaming
   Fixup fx = p.fx;
   fx.part = reinterpret_cast<float*>(smem + ring_smem_bytes(p.nst));
   uint8_t* xs = smem + base_smem_bytes(p.nst, p.x.ntok);
+  gemv_mark(p.trace, 1);
   pdl_wait();  // x, y and the split-K workspace belong to the stream's order from here
+  gemv_mark(p.trace, 2);
   stage_frags<NCOLS, SPLIT>(xs, p.m.KT, p.x);
+  ring.fill_rest();
   consumers_sync();
+  gemv_mark(p.trace, 3);
   if (!consume_range<NCOLS, SPLIT, FAST>(ring, p.m, u0, u1, xs, fx, p.x.ntok, p.epi, p.status))
     ring.drain();
+  gemv_mark(p.trace, 4);
   cta_fixup(pt, &wr[0][0], fx, p.x.ntok, p.epi);
+  gemv_mark(p.trace, 5);
 }
 
 // ===========================================================================
@@ -370,6 +394,7 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) gemv_kernel(const GemvParam
 struct FfnParams {
   Q4Mat gu;
   Q4Mat dn;
+  Partition ptA, ptB;   // gate/up (row-aligned) and down splits, host-built for the grid
   uint32_t H;
   uint32_t I;
   int fn;
@@ -699,20 +724,18 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_kernel(const FfnParams 
   constexpr uint32_t NTHR = kConsumerWarps * 32;
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const Partition ptA = Partition::make(p.gu.RT, p.gu.KT, gridDim.x, true);
-  const Partition ptB = Partition::make(p.dn.RT, p.dn.KT, gridDim.x);
+  const Partition& ptA = p.ptA;
+  const Partition& ptB = p.ptB;
   __shared__ WorkList wl[kConsumerWarps];
   __shared__ uint32_t wr[kConsumerWarps][4];  // per warp: gate/up [u0, u1), down [u0, u1)
   Shape::init_barriers(smem, p.nst);
-  uint64_t wa0, wa1, wb0, wb1;
-  ptA.warp_range(blockIdx.x, warp, wa0, wa1);
-  ptB.warp_range(blockIdx.x, warp, wb0, wb1);
-  const uint32_t a0 = static_cast<uint32_t>(wa0), a1 = static_cast<uint32_t>(wa1);
-  const uint32_t b0 = static_cast<uint32_t>(wb0), b1 = static_cast<uint32_t>(wb1);
+  uint32_t a0, a1, b0, b1;
+  ptA.warp_range(blockIdx.x, warp, a0, a1);
+  ptB.warp_range(blockIdx.x, warp, b0, b1);
   if (lane == 0) {
     wl[warp] = WorkList{p.gu.units + static_cast<size_t>(a0) * kUnitBytes,
                         p.dn.units + static_cast<size_t>(b0) * kUnitBytes, a1 - a0, b1 - b0,
-                        a0 % p.gu.KT, b0 % p.dn.KT, p.gu.KT, p.dn.KT};
+                        a0 - ptA.kt.div(a0) * p.gu.KT, b0 - ptB.kt.div(b0) * p.dn.KT, p.gu.KT, p.dn.KT};
     wr[warp][0] = a0;
     wr[warp][1] = a1;
     wr[warp][2] = b0;
@@ -822,6 +845,7 @@ struct StackParams {
   const LayerW* layers;
   uint32_t L;
   Q4Mat gu, dn;           // per-layer shapes (RT, KT); units / scale_mul come from layers
+  Partition ptA, ptB;     // gate/up (row-aligned) and down splits, host-built for the grid
   uint32_t H, I;
   int fn;
   int ntok;
@@ -1006,21 +1030,17 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const __gr
   __shared__ StackWork sw[kConsumerWarps];
   __shared__ unsigned long long xbase_s;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const Partition ptA = Partition::make(p.gu.RT, p.gu.KT, gridDim.x, true);
-  const Partition ptB = Partition::make(p.dn.RT, p.dn.KT, gridDim.x);
+  const Partition& ptA = p.ptA;
+  const Partition& ptB = p.ptB;
   Shape::init_barriers(smem, p.nst);
   const unsigned long long bar_base = threadIdx.x == 0 ? grid_base(p.bar, gridDim.x) : 0ull;
   if (TP && threadIdx.x == 0) xbase_s = peer_base(p.xr[p.rank], p.world);
   if (lane == 0) {
-    uint64_t a0, a1, b0, b1;
-    ptA.warp_range(blockIdx.x, warp, a0, a1);
-    ptB.warp_range(blockIdx.x, warp, b0, b1);
     uint32_t* w = wk[warp];
-    w[0] = static_cast<uint32_t>(a0);
-    w[1] = static_cast<uint32_t>(a1);
-    w[2] = static_cast<uint32_t>(b0);
-    w[3] = static_cast<uint32_t>(b1);
-    sw[warp] = StackWork{p.layers, p.L, w[0], w[1] - w[0], w[2], w[3] - w[2], p.gu.KT, p.dn.KT};
+    ptA.warp_range(blockIdx.x, warp, w[0], w[1]);
+    ptB.warp_range(blockIdx.x, warp, w[2], w[3]);
+    sw[warp] = StackWork{p.layers, p.L, w[0], w[1] - w[0], w[2], w[3] - w[2], p.gu.KT, p.dn.KT,
+                         w[0] - ptA.kt.div(w[0]) * p.gu.KT, w[2] - ptB.kt.div(w[2]) * p.dn.KT};
   }
   // Down row tiles -> the CTAs holding them (one CTA: `down` has the row;
   // several: the glue sums their partials), and each CTA's first row tile.
@@ -1028,11 +1048,10 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const __gr
   uint32_t* span = reinterpret_cast<uint32_t*>(split + p.dn.RT);
   uint32_t* cfirst = span + p.dn.RT;
   for (uint32_t r = threadIdx.x; r < p.dn.RT; r += blockDim.x) {
-    const uint64_t rb = static_cast<uint64_t>(r) * p.dn.KT;
+    const uint32_t rb = r * p.dn.KT;
     span[r] = ptB.aligned ? 0u : (ptB.cta_of_unit(rb) | (ptB.cta_of_unit(rb + p.dn.KT - 1) << 16));
   }
-  for (uint32_t c = threadIdx.x; c < gridDim.x; c += blockDim.x)
-    cfirst[c] = static_cast<uint32_t>(ptB.cta_begin(c) / p.dn.KT);
+  for (uint32_t c = threadIdx.x; c < gridDim.x; c += blockDim.x) cfirst[c] = ptB.kt.div(ptB.cta_begin(c));
   __syncthreads();
   for (uint32_t r = threadIdx.x; r < p.dn.RT; r += blockDim.x) {
     const uint32_t clo = span[r] & 0xFFFFu, chi = span[r] >> 16;
@@ -1052,12 +1071,12 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_stack_kernel(const __gr
   uint32_t prow0 = 0, prow1 = 0, xpar0 = 0;
   unsigned long long xbase = 0;
   if (TP) {
-    const uint64_t c0 = ptB.cta_begin(blockIdx.x), c1 = ptB.cta_begin(blockIdx.x + 1);
-    prow0 = static_cast<uint32_t>((c0 + p.dn.KT - 1) / p.dn.KT);
-    prow1 = static_cast<uint32_t>(c1 / p.dn.KT);
+    const uint32_t c0 = ptB.cta_begin(blockIdx.x), c1 = ptB.cta_begin(blockIdx.x + 1);
+    prow0 = ptB.kt.div(c0 + p.dn.KT - 1);
+    prow1 = ptB.kt.div(c1);
     if (prow1 < prow0) prow1 = prow0;
     xbase = xbase_s;
-    xpar0 = static_cast<uint32_t>(xbase / p.world) & 1u;
+    xpar0 = static_cast<uint32_t>(div_counter(xbase, p.world)) & 1u;
   }
   const uint32_t* my = wk[warp];
   ConsumerRing<kUnitsPerStage, StackWork> ring;

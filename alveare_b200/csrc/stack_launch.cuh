@@ -13,6 +13,10 @@ constexpr int kStackMaxTokens = 4;
 template <int NT, bool FAST, bool TP>
 int launch_stack_t(alv_ctx* ctx, StackParams p, cudaStream_t st) {
   const uint32_t nctas = static_cast<uint32_t>(ctx->num_sms);
+  if (!Partition::fits(p.gu.RT, p.gu.KT) || !Partition::fits(p.dn.RT, p.dn.KT))
+    return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn_stack: matrix too large for one launch's partition");
+  p.ptA = Partition::make(p.gu.RT, p.gu.KT, nctas, true);
+  p.ptB = Partition::make(p.dn.RT, p.dn.KT, nctas);
   const size_t other = stack_smem_bytes(0, p.gu.KT, p.dn.KT, NT, p.H, p.ntok, p.dn.RT, nctas);
   p.nst = ring_stages(other);
   if (!p.nst) return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn_stack: H, I or ntok too large for shared memory");

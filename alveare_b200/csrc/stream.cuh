@@ -60,22 +60,33 @@ struct Q4Mat {
   float scale_mul;       // 2^je (fast) or 1 (generic)
 };
 
-// Contiguous split of U units over W warps: warp w owns [start(w), start(w+1)).
-__host__ __device__ __forceinline__ uint64_t range_start(uint64_t w, uint64_t U, uint64_t W) {
-  return w * U / W;
-}
-// Participating warps for U units of a matrix with KT k tiles: every warp
-// owns >= 1 unit, and >= ceil(KT/16) units.
-__host__ __device__ __forceinline__ uint64_t effective_warps(uint64_t Wtot, uint64_t U, uint64_t KT) {
-  const uint64_t min_units = (KT + 15) / 16;
-  uint64_t w = U / (min_units ? min_units : 1);
-  if (w < 1) w = 1;
-  return w < Wtot ? w : Wtot;
-}
-// The warp whose range contains unit u.
-__host__ __device__ __forceinline__ uint32_t warp_of_unit(uint64_t u, uint64_t U, uint64_t W) {
-  return static_cast<uint32_t>(((u + 1) * W - 1) / U);
-}
+// Round-down division of 32-bit numerators by a divisor d >= 1 fixed at
+// launch: one multiply-high, an add, a subtract and two shifts instead of the
+// software division loop (Granlund and Montgomery, "Division by invariant
+// integers using multiplication", PLDI 1994, section 4): with l = ceil(log2 d)
+// and m = floor(2^32 (2^l - d) / d) + 1, t = mulhi(m, n) gives
+// n / d = (t + ((n - t) >> min(l, 1))) >> max(l - 1, 0).  Built on the host.
+struct FastDiv {
+  uint32_t d, m, s1, s2;
+  __host__ static FastDiv make(uint32_t d) {
+    FastDiv f{};
+    f.d = d ? d : 1;
+    uint32_t l = 0;
+    while ((uint64_t{1} << l) < f.d) ++l;
+    f.m = static_cast<uint32_t>((uint64_t{1} << 32) * ((uint64_t{1} << l) - f.d) / f.d + 1);
+    f.s1 = l < 1 ? l : 1;
+    f.s2 = l > 1 ? l - 1 : 0;
+    return f;
+  }
+  __host__ __device__ __forceinline__ uint32_t div(uint32_t n) const {
+#ifdef __CUDA_ARCH__
+    const uint32_t t = __umulhi(m, n);
+#else
+    const uint32_t t = static_cast<uint32_t>((static_cast<uint64_t>(m) * n) >> 32);
+#endif
+    return (t + ((n - t) >> s1)) >> s2;
+  }
+};
 
 // How a matrix's RT x KT units are split over the grid: CTA c owns one
 // contiguous unit range and its warps split that range.  Row-aligned when
@@ -83,47 +94,82 @@ __host__ __device__ __forceinline__ uint32_t warp_of_unit(uint64_t u, uint64_t U
 // reduction then never leaves the CTA) or when every CTA can take whole row
 // tiles at < 1/32 imbalance (then no row tile spans two CTAs and the split-K
 // reduction stays in shared memory); otherwise unit-balanced: W
-// participating warps numbered CTA-major, warp gw owning [gw*U/W, (gw+1)*U/W).
-// A row-aligned split of RT < nctas row tiles leaves CTAs without work.
+// participating warps numbered CTA-major, warp gw owning
+// [floor(gw U / W), floor((gw + 1) U / W)), W chosen so that every warp owns
+// >= 1 and >= ceil(KT / 16) units.  A row-aligned split of RT < nctas row
+// tiles leaves CTAs without work.
+//
+// Built on the host for the launch's grid (every divisor fixed then, so the
+// device side is 32-bit multiply-high arithmetic: the kernels evaluate these
+// at their start and in every split-K reduction, on the critical path).
+// Limits (checked by make): U < 2^28 units, RT < 2^24 row tiles.
 struct Partition {
-  uint64_t U, W;
   uint32_t RT, KT, nctas, aligned;
+  uint32_t U, W;        // units; participating warps (unit-balanced)
+  uint32_t qUW, rUW;    // U / W and U % W
+  float invU;           // 1 / U, for the warp-of-unit estimate
+  FastDiv kt, nct, wd;  // division by KT, nctas and W
 
-  __host__ __device__ static Partition make(uint32_t RT, uint32_t KT, uint32_t nctas, bool row_aligned = false) {
-    Partition p;
+  __host__ static bool fits(uint64_t RT, uint64_t KT) { return RT < (1u << 24) && RT * KT < (1u << 28); }
+  __host__ static Partition make(uint32_t RT, uint32_t KT, uint32_t nctas, bool row_aligned = false) {
+    Partition p{};
     p.RT = RT;
     p.KT = KT;
     p.nctas = nctas;
-    p.U = static_cast<uint64_t>(RT) * KT;
+    p.U = RT * KT;
     const uint64_t per = (static_cast<uint64_t>(RT) + nctas - 1) / nctas;
     p.aligned = row_aligned || (RT >= nctas && per * nctas * 32 <= static_cast<uint64_t>(RT) * 33);
-    p.W = effective_warps(static_cast<uint64_t>(nctas) * kWarpsPerCtaS, p.U, KT);
+    const uint32_t min_units = (KT + 15) / 16;
+    uint64_t w = p.U / (min_units ? min_units : 1);
+    if (w < 1) w = 1;
+    const uint64_t wtot = static_cast<uint64_t>(nctas) * kWarpsPerCtaS;
+    p.W = static_cast<uint32_t>(w < wtot ? w : wtot);
+    p.qUW = p.U / p.W;
+    p.rUW = p.U % p.W;
+    p.invU = p.U ? 1.0f / static_cast<float>(p.U) : 0.f;
+    p.kt = FastDiv::make(KT);
+    p.nct = FastDiv::make(nctas);
+    p.wd = FastDiv::make(p.W);
     return p;
   }
+  // First unit of warp gw of the unit-balanced split: floor(gw U / W), as
+  // gw (U / W) + (gw (U % W)) / W (gw (U % W) < W^2 < 2^32).
+  __host__ __device__ __forceinline__ uint32_t range_start(uint32_t gw) const { return gw * qUW + wd.div(gw * rUW); }
   // First unit of CTA c (c = nctas gives U).
-  __host__ __device__ uint64_t cta_begin(uint32_t c) const {
-    if (aligned) return static_cast<uint64_t>(c) * RT / nctas * KT;
-    const uint64_t gw = static_cast<uint64_t>(c) * kWarpsPerCtaS;
-    return range_start(gw < W ? gw : W, U, W);
+  __host__ __device__ __forceinline__ uint32_t cta_begin(uint32_t c) const {
+    if (aligned) return nct.div(c * RT) * KT;
+    const uint32_t gw = c * kWarpsPerCtaS;
+    return range_start(gw < W ? gw : W);
   }
   // Units [u0, u1) of warp w of CTA c (possibly empty).
-  __host__ __device__ void warp_range(uint32_t c, uint32_t w, uint64_t& u0, uint64_t& u1) const {
+  __host__ __device__ __forceinline__ void warp_range(uint32_t c, uint32_t w, uint32_t& u0, uint32_t& u1) const {
     if (aligned) {
-      const uint64_t c0 = cta_begin(c), len = cta_begin(c + 1) - c0;
+      const uint32_t c0 = cta_begin(c), len = cta_begin(c + 1) - c0;
       u0 = c0 + len * w / kWarpsPerCtaS;
       u1 = c0 + len * (w + 1) / kWarpsPerCtaS;
       return;
     }
-    const uint64_t gw = static_cast<uint64_t>(c) * kWarpsPerCtaS + w;
+    const uint32_t gw = c * kWarpsPerCtaS + w;
     if (gw >= W) {
       u0 = u1 = U;
       return;
     }
-    u0 = range_start(gw, U, W);
-    u1 = range_start(gw + 1, U, W);
+    u0 = range_start(gw);
+    u1 = range_start(gw + 1);
+  }
+  // The warp whose range holds unit u (unit-balanced): the gw with
+  // range_start(gw) <= u < range_start(gw + 1), i.e. floor(((u + 1) W - 1) / U);
+  // a float estimate corrected exactly with 64-bit products.
+  __host__ __device__ __forceinline__ uint32_t warp_of_unit(uint32_t u) const {
+    const uint64_t n = static_cast<uint64_t>(u + 1) * W - 1;
+    uint32_t q = static_cast<uint32_t>(static_cast<float>(n) * invU);
+    if (q >= W) q = W - 1;
+    while (q > 0 && static_cast<uint64_t>(q) * U > n) --q;
+    while (q + 1 < W && static_cast<uint64_t>(q + 1) * U <= n) ++q;
+    return q;
   }
   // CTA holding unit u (unit-balanced partitions only).
-  __host__ __device__ uint32_t cta_of_unit(uint64_t u) const { return warp_of_unit(u, U, W) / kWarpsPerCtaS; }
+  __host__ __device__ __forceinline__ uint32_t cta_of_unit(uint32_t u) const { return warp_of_unit(u) / kWarpsPerCtaS; }
 };
 
 // ---------------------------------------------------------------------------
@@ -263,6 +309,7 @@ struct StackWork {
   const LayerW* layers;
   uint32_t L, a0, na, b0, nb;
   uint32_t KTA, KTB;   // k tiles per row tile of gate/up and of down
+  uint32_t kta, ktb;   // k tile of unit a0 (a0 % KTA) and of unit b0
   __device__ uint32_t nseg() const { return 2 * L; }
   __device__ void get(uint32_t i, const uint8_t*& base, uint32_t& n, uint32_t& KT, uint32_t& kt) const {
     const LayerW* lw = layers + (i >> 1);
@@ -271,13 +318,13 @@ struct StackWork {
              static_cast<size_t>(b0) * kUnitBytes;
       n = nb;
       KT = KTB;
-      kt = b0 % KTB;
+      kt = ktb;
     } else {
       base = reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(&lw->gu))) +
              static_cast<size_t>(a0) * kUnitBytes;
       n = na;
       KT = KTA;
-      kt = a0 % KTA;
+      kt = kta;
     }
   }
 };
@@ -354,11 +401,16 @@ struct ConsumerRing {
   uint32_t stage, phase;    // current stage and the parity of its next fill
   uint32_t inflight;        // groups copied and not yet released
   uint32_t cp_left;         // units of the sequence not yet copied
+  uint32_t primed;          // stages issued by setup()
   Cursor cur;
   const Seq* seq;           // this warp's work sequence (shared memory)
 
-  // total = units of the whole sequence.  Issues the first groups (all lanes call).
-  __device__ void setup(uint8_t* smem, uint32_t nst_, int c, uint32_t total, const Seq* seq_) {
+  // total = units of the whole sequence.  Issues the copies of the first
+  // `first` stages (all of them by default; all lanes call).  A kernel that
+  // must read something latency-critical right after it starts (its input
+  // vector) primes one stage, reads its input while only that much of its own
+  // weight stream is queued ahead of it, then calls fill_rest().
+  __device__ void setup(uint8_t* smem, uint32_t nst_, int c, uint32_t total, const Seq* seq_, uint32_t first = ~0u) {
     nst = nst_;
     ring_saddr = smem_u32(RingShape<UPS>::ring(smem, nst, c));
     full_saddr = smem_u32(RingShape<UPS>::full(smem, nst, c));
@@ -366,7 +418,13 @@ struct ConsumerRing {
     cp_left = total;
     cur = Cursor{nullptr, 0, 0, 1, 0};
     seq = seq_;
-    for (uint32_t s = 0; s < nst; ++s) refill(s);
+    primed = first < nst ? first : nst;
+    for (uint32_t s = 0; s < primed; ++s) refill(s);
+  }
+  // Issue the stages setup() held back (before the first release()).
+  __device__ __forceinline__ void fill_rest() {
+    for (uint32_t s = primed; s < nst; ++s) refill(s);
+    primed = nst;
   }
   // Copy the next group into stage s (a single bulk copy).  The stage's
   // previous contents were loaded into registers and consumed by the warp's
@@ -622,14 +680,14 @@ __device__ void cta_fixup(const Partition& pt, const uint32_t* wr, const Fixup& 
   // wr[4 * w + 0 / 1]: unit range [u0, u1) of warp w of this CTA (shared memory)
   consumers_sync();  // every warp's partials are in shared memory
   const uint32_t KT = pt.KT, c = blockIdx.x;
-  const uint64_t c0 = pt.cta_begin(c), c1 = pt.cta_begin(c + 1);
+  const uint32_t c0 = pt.cta_begin(c), c1 = pt.cta_begin(c + 1);
   if (c0 >= c1) return;
-  const uint32_t r_lo = static_cast<uint32_t>(c0 / KT), r_hi = static_cast<uint32_t>((c1 - 1) / KT);
+  const uint32_t r_lo = pt.kt.div(c0), r_hi = pt.kt.div(c1 - 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const size_t slot_floats = static_cast<size_t>(ntok) * 16;
   for (uint32_t r = r_lo + warp; r <= r_hi; r += kWarpsPerCtaS) {
-    const uint64_t rb = static_cast<uint64_t>(r) * KT, re = rb + KT;
-    const uint64_t ib = rb > c0 ? rb : c0, ie = re < c1 ? re : c1;  // this CTA's part of the row tile
+    const uint32_t rb = r * KT, re = rb + KT;
+    const uint32_t ib = rb > c0 ? rb : c0, ie = re < c1 ? re : c1;  // this CTA's part of the row tile
     const bool inside = rb >= c0 && re <= c1;
     // Contributing warps (contiguous): ranges that meet [ib, ie).
     uint32_t w_lo = kWarpsPerCtaS, w_hi = 0;
@@ -651,7 +709,7 @@ __device__ void cta_fixup(const Partition& pt, const uint32_t* wr, const Fixup& 
       float vg = 0.f, vg8 = 0.f;
       for (uint32_t w = w_lo; w <= w_hi; ++w) {
         if (!(wr[4 * w] < wr[4 * w + 1] && wr[4 * w] < ie && wr[4 * w + 1] > ib)) continue;  // an empty warp between contributors
-        const float* src = fx.part + (static_cast<size_t>(w) * 2 + (r == wr[4 * w] / KT ? 0 : 1)) * slot_floats;
+        const float* src = fx.part + (static_cast<size_t>(w) * 2 + (r == pt.kt.div(wr[4 * w]) ? 0 : 1)) * slot_floats;
         vg += src[tok * 16 + g];
         vg8 += src[tok * 16 + g + 8];
       }
@@ -679,7 +737,7 @@ __device__ void cta_fixup(const Partition& pt, const uint32_t* wr, const Fixup& 
       const int g = e & 7, tok = e >> 3;
       float vg = 0.f, vg8 = 0.f;
       for (uint32_t cc = cta_lo; cc <= cta_hi; ++cc) {
-        const uint32_t cfirst = static_cast<uint32_t>(pt.cta_begin(cc) / KT);
+        const uint32_t cfirst = pt.kt.div(pt.cta_begin(cc));
         const float* src = fx.ws + (static_cast<size_t>(cc) * 2 + (r == cfirst ? 0 : 1)) * slot_floats;
         vg += __ldcg(src + tok * 16 + g);
         vg8 += __ldcg(src + tok * 16 + g + 8);

@@ -312,8 +312,10 @@ int alv_gemv_noalloc(alv_ctx* ctx, alv_handle h, int ntok, const void* x, int x_
  * start, [1]-[5] as above, [6] the layer's last barrier passed, [7] / [8]
  * gate/up / down units streamed, before the split-K reduction; inside its
  * glue [9] down loaded, [10] / [11] the norms of down / x reduced, [12] the
- * normalized x written).  Slots [13]-[15] are unused.  NULL turns tracing
- * off (the default). */
+ * normalized x written).  Slots [13]-[15] are unused.  alv_gemv launches
+ * write [0] start, [1] weights requested, [2] the previous kernel in the
+ * stream finished, [3] x staged, [4] warp 0's units consumed, [5] split-K
+ * reduction done.  NULL turns tracing off (the default). */
 int alv_set_trace(alv_ctx* ctx, uint64_t* trace);
 
 /* ---- host-buffer convenience (synchronous, like NpuRegistry::run_gemv) ---- */
