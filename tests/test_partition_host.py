@@ -18,19 +18,19 @@ PROGRAM = r"""
 using namespace alv;
 int check(uint32_t RT, uint32_t KT, uint32_t nctas) {
   const Partition p = Partition::make(RT, KT, nctas);
-  uint64_t next = 0;
+  uint32_t next = 0;
   for (uint32_t c = 0; c < nctas; ++c) {
-    const uint64_t c0 = p.cta_begin(c), c1 = p.cta_begin(c + 1);
+    const uint32_t c0 = p.cta_begin(c), c1 = p.cta_begin(c + 1);
     if (c0 != next && c0 < p.U) return 1;
-    uint64_t w_next = c0;
+    uint32_t w_next = c0;
     for (uint32_t w = 0; w < kWarpsPerCtaS; ++w) {
-      uint64_t u0, u1;
+      uint32_t u0, u1;
       p.warp_range(c, w, u0, u1);
       if (u0 == u1) continue;
       if (u0 != w_next || u1 < u0) return 2;
       w_next = u1;
       if (!p.aligned)
-        for (uint64_t u : {u0, u1 - 1})
+        for (uint32_t u : {u0, u1 - 1})
           if (p.cta_of_unit(u) != c) return 3;
     }
     if (c0 < c1 && w_next != c1) return 4;
