@@ -6,17 +6,20 @@ namespace alv {
 namespace {
 
 // Ring stages a gemv CTA requests before it stages x.  Its x loads queue
-// behind every byte already requested from HBM, so all stages up front
-// (about the whole matrix for decode shapes) make x arrive late and stall
-// the stream; one stage per warp keeps HBM busy while x is fetched.
-constexpr uint32_t kGemvFirstStages = 1;
+// behind every byte already requested from HBM, so for a large matrix all
+// stages up front (about the whole matrix for decode shapes) make x arrive
+// late and stall the stream: one stage per warp keeps HBM busy while x is
+// fetched.  Matrices up to kGemvPrimeAllBytes request every stage up front
+// (their whole stream is a few microseconds of HBM time, and a warp's second
+// group would otherwise wait a full round trip after x is staged).
+constexpr size_t kGemvPrimeAllBytes = size_t{16} << 20;
 
 template <int NCOLS, bool SPLIT, bool FAST>
 int launch_gemv_t(alv_ctx* ctx, GemvParams p, cudaStream_t st, bool pdl) {
   const size_t other = part_bytes(p.x.ntok) + frag_bytes(p.m.KT, NCOLS);
   p.nst = ring_stages(other);
   if (!p.nst) return fail(ctx, ALV_ERR_UNSUPPORTED, "gemv: K too large for the shared-memory fragment stage");
-  p.first = kGemvFirstStages;
+  p.first = static_cast<size_t>(p.m.RT) * p.m.KT * kUnitBytes <= kGemvPrimeAllBytes ? p.nst : 1;
   // Row-aligned unless there are too few row tiles to keep the SMs busy: a
   // row tile split between CTAs costs the finishing CTA a fence, an atomic
   // and a round trip at the end, more than the imbalance of whole rows.

@@ -356,7 +356,10 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) gemv_kernel(const GemvParam
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const Partition& pt = p.pt;
   gemv_mark(p.trace, 0);
-  Shape::init_barriers(smem, p.nst);
+  // Each warp starts its own weight stream as soon as it can: its ring's
+  // barriers, range and work list are its own (the CTA syncs before it
+  // stages x, which every warp reads).
+  Shape::init_warp_barriers(smem, p.nst, warp);
   uint32_t u0, u1;
   pt.warp_range(blockIdx.x, warp, u0, u1);
   if (lane == 0) {
@@ -365,10 +368,10 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) gemv_kernel(const GemvParam
     wr[warp][0] = u0;
     wr[warp][1] = u1;
   }
-  __syncthreads();
-  pdl_trigger();
+  __syncwarp();
   ConsumerRing<kUnitsPerStage, WorkList> ring;
   ring.setup(smem, p.nst, warp, u1 - u0, &wl[warp], p.first);  // weights start streaming
+  pdl_trigger();
   Fixup fx = p.fx;
   fx.part = reinterpret_cast<float*>(smem + ring_smem_bytes(p.nst));
   uint8_t* xs = smem + base_smem_bytes(p.nst, p.x.ntok);

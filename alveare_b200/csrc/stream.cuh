@@ -349,6 +349,15 @@ struct RingShape {
     for (uint32_t i = threadIdx.x; i < kConsumerWarps * nst; i += blockDim.x) mbar_init(&f[i], 1);
     fence_mbar_init();
   }
+  // One warp: initialize its own ring's barriers (no CTA-wide sync needed
+  // before the warp issues its first copies).
+  __device__ static void init_warp_barriers(uint8_t* smem, uint32_t nst, int c) {
+    uint64_t* f = full(smem, nst, c);
+    const uint32_t lane = threadIdx.x & 31;
+    if (lane < nst) mbar_init(&f[lane], 1);
+    fence_mbar_init();
+    __syncwarp();
+  }
 };
 
 // Lane 0 only (pred): arm `bar` for `bytes` and start one bulk copy of them.
@@ -685,34 +694,44 @@ __device__ void cta_fixup(const Partition& pt, const uint32_t* wr, const Fixup& 
   const uint32_t r_lo = pt.kt.div(c0), r_hi = pt.kt.div(c1 - 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const size_t slot_floats = static_cast<size_t>(ntok) * 16;
+  // Lane w holds warp w's range and the row its slot 0 belongs to, so the
+  // contributors of a row tile are one ballot and every partial load of an
+  // element is in flight at once (a loop over the warps would pay one
+  // shared-memory round trip per warp and step).
+  const uint32_t lu0 = lane < kConsumerWarps ? wr[4 * lane] : 0u;
+  const uint32_t lu1 = lane < kConsumerWarps ? wr[4 * lane + 1] : 0u;
+  const uint32_t lrow0 = pt.kt.div(lu0);
   for (uint32_t r = r_lo + warp; r <= r_hi; r += kWarpsPerCtaS) {
     const uint32_t rb = r * KT, re = rb + KT;
     const uint32_t ib = rb > c0 ? rb : c0, ie = re < c1 ? re : c1;  // this CTA's part of the row tile
     const bool inside = rb >= c0 && re <= c1;
-    // Contributing warps (contiguous): ranges that meet [ib, ie).
-    uint32_t w_lo = kWarpsPerCtaS, w_hi = 0;
-    bool whole = false;
-    for (uint32_t w = 0; w < kWarpsPerCtaS; ++w) {
-      const uint32_t u0 = wr[4 * w], u1 = wr[4 * w + 1];
-      if (u0 < u1 && u0 < ie && u1 > ib) {  // a non-empty range that meets the tile
-        w_lo = w < w_lo ? w : w_lo;
-        w_hi = w;
-        whole = u0 <= rb && u1 >= re;
-      }
-    }
-    if (w_lo > w_hi) continue;
-    if (inside && w_lo == w_hi && whole) continue;  // one warp held the whole tile: applied already
+    // Contributing warps (contiguous): non-empty ranges that meet [ib, ie).
+    const uint32_t meets = __ballot_sync(0xffffffffu, lu0 < lu1 && lu0 < ie && lu1 > ib);
+    if (!meets) continue;
+    const bool whole = __shfl_sync(0xffffffffu, lu0 <= rb && lu1 >= re, 31 - __clz(meets));
+    if (inside && __popc(meets) == 1 && whole) continue;  // one warp held the whole tile: applied already
+    const uint32_t slot1 = __ballot_sync(0xffffffffu, r != lrow0);  // warp w parked row r in its slot 1
     const int cslot = (r == r_lo) ? 0 : 1;
     float* cpart = fx.ws + (static_cast<size_t>(c) * 2 + cslot) * slot_floats;
     for (uint32_t e = lane; e < 8u * ntok; e += 32) {
       const int g = e & 7, tok = e >> 3;
-      float vg = 0.f, vg8 = 0.f;
-      for (uint32_t w = w_lo; w <= w_hi; ++w) {
-        if (!(wr[4 * w] < wr[4 * w + 1] && wr[4 * w] < ie && wr[4 * w + 1] > ib)) continue;  // an empty warp between contributors
-        const float* src = fx.part + (static_cast<size_t>(w) * 2 + (r == pt.kt.div(wr[4 * w]) ? 0 : 1)) * slot_floats;
-        vg += src[tok * 16 + g];
-        vg8 += src[tok * 16 + g + 8];
+      float pg[kConsumerWarps], pg8[kConsumerWarps];
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        pg[w] = pg8[w] = 0.f;
+        if ((meets >> w) & 1u) {
+          const float* src = fx.part + (static_cast<size_t>(w) * 2 + ((slot1 >> w) & 1u)) * slot_floats;
+          pg[w] = src[tok * 16 + g];
+          pg8[w] = src[tok * 16 + g + 8];
+        }
       }
+      float vg = 0.f, vg8 = 0.f;  // warp order
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w)
+        if ((meets >> w) & 1u) {
+          vg += pg[w];
+          vg8 += pg8[w];
+        }
       if (inside) {
         epi.apply(r, g, tok, vg, vg8);
       } else if constexpr (DEFER) {  // the epilogue may pre-scale parked partials
