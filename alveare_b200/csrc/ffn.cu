@@ -22,12 +22,18 @@ int launch_ffn_t(alv_ctx* ctx, FfnParams p, cudaStream_t st) {
   p.ptB = Partition::make(p.dn.RT, p.dn.KT, nctas);
   p.nst = ring_stages(other);
   if (!p.nst) return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn: H or I too large for the shared-memory fragment stage");
+  // As for gemv: small FFNs request every stage at once, large ones one stage
+  // per warp before the inputs are staged.
+  const size_t wbytes = (static_cast<size_t>(p.gu.RT) * p.gu.KT + static_cast<size_t>(p.dn.RT) * p.dn.KT) * kUnitBytes;
+  p.first = wbytes <= (size_t{16} << 20) ? p.nst : 1;
   const size_t smem = ring_smem_bytes(p.nst) + other;
   auto k = ffn_kernel<NT, SPLIT, FAST>;
   // Grid barrier between the phases: every CTA must be resident at once.
   int rc = prepare_kernel(ctx, k, smem, kThreadsPerCta, ctx->num_sms);
   if (rc) return rc;
-  return launch_cooperative(ctx, k, p, ctx->num_sms, kThreadsPerCta, smem, st);
+  // Programmatic dependent launch: the weight stream starts while the
+  // previous kernel finishes (the kernel waits before it reads its inputs).
+  return launch_cooperative(ctx, k, p, ctx->num_sms, kThreadsPerCta, smem, st, true);
 }
 
 template <bool FAST>

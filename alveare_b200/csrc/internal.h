@@ -199,17 +199,19 @@ int prepare_kernel(alv_ctx* ctx, K kernel, size_t smem, int threads = 0, int gri
 // the launch), instead of the grid barrier assuming it.
 template <class P>
 int launch_cooperative(alv_ctx* ctx, void (*kernel)(P), const P& p, unsigned grid, unsigned threads, size_t smem,
-                       cudaStream_t st) {
+                       cudaStream_t st, bool pdl = false) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl ? 2 : 1;
   ALV_CUDA(ctx, cudaLaunchKernelEx(&cfg, kernel, p));
   return ALV_OK;
 }

@@ -172,37 +172,13 @@ __device__ __forceinline__ unsigned long long div_counter(unsigned long long n, 
   return q;
 }
 
-// One atomic per CTA: the k-th use of the barrier completes when the counter
-// reaches k * nblocks; waiters poll the counter itself.  Correct across
-// launches because every launch uses it a whole number of times with the
-// same grid, so the counter always resumes at a multiple of nblocks.
-inline __device__ bool grid_barrier(GridBar* gb, uint32_t nblocks, uint32_t* status) {
-  consumers_sync();
-  int ok = 1;
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const unsigned long long arrived = atomicAdd(&gb->count, 1ull);
-    const unsigned long long target = (div_counter(arrived, nblocks) + 1) * nblocks;
-    volatile unsigned long long* vc = &gb->count;
-    if (*vc < target) {
-      const unsigned long long t0 = globaltimer_ns();
-      while (*vc < target) {
-        if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
-          atomicOr(status, kStatusGridTimeout);
-          ok = 0;
-          break;
-        }
-      }
-    }
-    __threadfence();
-  }
-  return consumers_and(ok != 0);
-}
-
-// Grid barrier for a kernel that passes it many times (the FFN stack): the
-// arrival is a fire-and-forget release reduction and the target is known in
-// advance, so a CTA pays one poll round trip, not an atomic's return trip
-// plus the poll.  `base` is the counter's value at launch, read once before
+// Grid barrier: the k-th use of the barrier by a launch completes when the
+// monotonic counter reaches base + k * nblocks.  The arrival is a
+// fire-and-forget release reduction and the target is known in advance, so
+// a CTA pays one poll round trip, not an atomic's return trip plus the poll.
+// Correct across launches because every launch uses it a whole number of
+// times with the same grid, so the counter always resumes at a multiple of
+// nblocks.  `base` is the counter's value at launch, read once before
 // the first arrival (grid_base); `epoch` counts this launch's barriers.
 __device__ __forceinline__ unsigned long long grid_base(GridBar* gb, uint32_t nblocks) {
   // At most nblocks - 1 arrivals of this launch can precede the read (the
@@ -408,6 +384,7 @@ struct FfnParams {
   const float* down_in;
   uint16_t* x_out;
   float eps;
+  uint32_t first;       // ring stages requested before the inputs are staged (the rest after)
   RowsEpi out;          // down projection output
   uint8_t* act;         // scratch: act in B-fragment order, frag_bytes(dn.KT, NT) bytes
   Fixup fxA, fxB;
@@ -731,7 +708,7 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_kernel(const FfnParams 
   const Partition& ptB = p.ptB;
   __shared__ WorkList wl[kConsumerWarps];
   __shared__ uint32_t wr[kConsumerWarps][4];  // per warp: gate/up [u0, u1), down [u0, u1)
-  Shape::init_barriers(smem, p.nst);
+  Shape::init_warp_barriers(smem, p.nst, warp);
   uint32_t a0, a1, b0, b1;
   ptA.warp_range(blockIdx.x, warp, a0, a1);
   ptB.warp_range(blockIdx.x, warp, b0, b1);
@@ -763,19 +740,25 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_kernel(const FfnParams 
     mbar_init(xbar, 1);
     fence_mbar_init();
   }
-  __syncthreads();
+  __syncwarp();
+  // Each warp starts its weight stream (its ring, range and work list are its
+  // own) while the previous kernel in the stream may still be finishing; the
+  // layer inputs, the split-K workspace and the barrier counter are touched
+  // only after griddepcontrol.wait.  Large FFNs request one stage per warp
+  // first, so the inputs do not queue behind the whole weight stream.
+  ConsumerRing<kUnitsPerStage, WorkList> ring;
+  ring.setup(smem, p.nst, warp, (a1 - a0) + (b1 - b0), &wl[warp], p.first);
+  pdl_trigger();
+  pdl_wait();
+  const unsigned long long bar_base = threadIdx.x == 0 ? grid_base(p.bar, gridDim.x) : 0ull;
+  __syncthreads();  // xbar initialized
   if (tma_in && threadIdx.x == 0) {
-    // The layer inputs go first, ahead of the weight stream.
     const uint64_t pol = l2_policy_evict_first();
     const uint32_t xb = static_cast<uint32_t>(glue_vals * 2), db = p.down_in ? static_cast<uint32_t>(glue_vals * 4) : 0;
     mbar_arrive_expect_tx(xbar, xb + db);
     bulk_g2s(xraw, p.x_in, xb, xbar, pol);
     if (db) bulk_g2s(draw, p.down_in, db, xbar, pol);
   }
-  pdl_trigger();
-  ConsumerRing<kUnitsPerStage, WorkList> ring;
-  ring.setup(smem, p.nst, warp, (a1 - a0) + (b1 - b0), &wl[warp]);
-  pdl_wait();
   trace_mark(p.trace, 0);
 
   // The act padding (k in [I, 64*dn.KT)) must read as zero in phase B.
@@ -802,6 +785,7 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_kernel(const FfnParams 
   } else {
     stage_frags<NCA, SPLIT>(xs, p.gu.KT, p.x);
   }
+  ring.fill_rest();
   consumers_sync();
   trace_mark(p.trace, 1);
 
@@ -812,7 +796,7 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) ffn_kernel(const FfnParams 
     consumers_sync();
     trace_mark(p.trace, 2);
   }
-  const bool bar_ok = grid_barrier(p.bar, gridDim.x, p.status);
+  const bool bar_ok = grid_barrier_epoch(p.bar, gridDim.x, bar_base, 1, p.status);
   trace_mark(p.trace, 3);
   if (!bar_ok || !consumers_and(ok)) {
     ring.drain();
