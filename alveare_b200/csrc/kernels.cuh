@@ -933,56 +933,84 @@ inline __device__ void push_down(const StackParams& p, uint32_t par, uint32_t ro
 // Tensor parallelism: sum the ranks' partial down projections of the
 // previous layer (their slots in this GPU's exchange region, complete after
 // the peer barrier) into dsum (fp32 [ntok][H], before the glue's bf16
-// rounding), every element as DownInX reads it -- each rank's whole-row value
-// or its CTA partials (pre-scaled) summed in CTA order, the ranks summed in
-// rank order -- but with element pairs loaded 8 bytes at a time and the
-// loads of up to four ranks in flight together (one element at a time would
-// wait one round trip per rank).
+// rounding), every element as the one-GPU glue reads it -- each rank's
+// whole-row value or its CTA partials (pre-scaled) summed in CTA order, the
+// ranks summed in rank order.  Memory-level parallelism is what matters:
+// a thread owns kQuads groups of four consecutive elements (16-byte loads)
+// and issues the loads of all of them, for two ranks at a time, before it
+// adds anything (more in flight makes the kernel spill around the call).
 static __device__ __noinline__ void tp_gather(const StackParams& p, uint32_t par, const uint2* split,
                                        const uint32_t* cfirst, const uint32_t* span, float* dsum) {
   constexpr uint32_t NTHR = kConsumerWarps * 32;
-  constexpr int WG = 4;                 // ranks per batch
+  constexpr int WG = 2;      // ranks per batch
+  constexpr int kQuads = 1;  // element quads per thread per pass
   const uint32_t H = p.H, ntok = static_cast<uint32_t>(p.ntok), W = p.world;
-  const uint32_t npairs = ntok * H / 2, sf = ntok * 16;
-  for (uint32_t pr = threadIdx.x; pr < npairs; pr += NTHR) {
-    const uint32_t e = 2 * pr, tok = e / H, h = e - tok * H, r = h >> 4;
-    const uint2 o = split[r];
-    const uint32_t el = tok * 16 + (h & 15);
-    float acc0 = 0.f, acc1 = 0.f;
-    for (uint32_t q0 = 0; q0 < W; q0 += WG) {
-      float2 a[WG], b[WG];
+  const uint32_t nquads = ntok * H / 4, sf = ntok * 16;
+  for (uint32_t base = 0; base < nquads; base += NTHR * kQuads) {
+    uint32_t eq[kQuads], rq[kQuads], elq[kQuads];
+    uint2 oq[kQuads];
+    float4 acc[kQuads];
 #pragma unroll
-      for (int qq = 0; qq < WG; ++qq) {
-        a[qq] = b[qq] = make_float2(0.f, 0.f);
-        if (q0 + qq >= W) continue;
-        const float* d = xslot_ptr(p, p.rank, par, q0 + qq);
-        if (o.x == ~0u) {
-          a[qq] = __ldcg(reinterpret_cast<const float2*>(d + e));
-        } else if (o.y != ~0u) {
-          a[qq] = __ldcg(reinterpret_cast<const float2*>(d + p.xws_off + o.x + el));
-          b[qq] = __ldcg(reinterpret_cast<const float2*>(d + p.xws_off + o.y + el));
-        } else {  // a row tile over three or more CTAs (small problems)
-          const uint32_t sp = span[r];
-          for (uint32_t c = sp & 0xFFFFu; c <= (sp >> 16); ++c) {
-            const float2 v = __ldcg(reinterpret_cast<const float2*>(
-                d + p.xws_off + (static_cast<size_t>(c) * 2 + (r == cfirst[c] ? 0 : 1)) * sf + el));
-            a[qq].x += v.x;
-            a[qq].y += v.y;
+    for (int i = 0; i < kQuads; ++i) {
+      const uint32_t q = base + i * NTHR + threadIdx.x;
+      eq[i] = 4 * q;
+      const uint32_t tok = q < nquads ? eq[i] / H : 0, h = eq[i] - tok * H;
+      rq[i] = h >> 4;
+      oq[i] = q < nquads ? split[rq[i]] : make_uint2(~0u, ~0u);
+      elq[i] = tok * 16 + (h & 15);
+      acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    for (uint32_t q0 = 0; q0 < W; q0 += WG) {
+      float4 a[kQuads][WG], b[kQuads][WG];
+#pragma unroll
+      for (int i = 0; i < kQuads; ++i)
+#pragma unroll
+        for (int qq = 0; qq < WG; ++qq) {
+          a[i][qq] = b[i][qq] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (q0 + qq >= W || base + i * NTHR + threadIdx.x >= nquads) continue;
+          const float* d = xslot_ptr(p, p.rank, par, q0 + qq);
+          const uint2 o = oq[i];
+          if (o.x == ~0u) {
+            a[i][qq] = __ldcg(reinterpret_cast<const float4*>(d + eq[i]));
+          } else if (o.y != ~0u) {
+            a[i][qq] = __ldcg(reinterpret_cast<const float4*>(d + p.xws_off + o.x + elq[i]));
+            b[i][qq] = __ldcg(reinterpret_cast<const float4*>(d + p.xws_off + o.y + elq[i]));
+          } else {  // a row tile over three or more CTAs (small problems)
+            const uint32_t sp = span[rq[i]];
+            for (uint32_t c = sp & 0xFFFFu; c <= (sp >> 16); ++c) {
+              const float4 v = __ldcg(reinterpret_cast<const float4*>(
+                  d + p.xws_off + (static_cast<size_t>(c) * 2 + (rq[i] == cfirst[c] ? 0 : 1)) * sf + elq[i]));
+              a[i][qq].x += v.x;
+              a[i][qq].y += v.y;
+              a[i][qq].z += v.z;
+              a[i][qq].w += v.w;
+            }
+          }
+        }
+#pragma unroll
+      for (int i = 0; i < kQuads; ++i) {
+        const bool two = oq[i].x != ~0u && oq[i].y != ~0u;
+#pragma unroll
+        for (int qq = 0; qq < WG; ++qq) {
+          const uint32_t q = q0 + qq;
+          if (q >= W) continue;
+          const float4 t = two ? make_float4(a[i][qq].x + b[i][qq].x, a[i][qq].y + b[i][qq].y,
+                                             a[i][qq].z + b[i][qq].z, a[i][qq].w + b[i][qq].w)
+                               : a[i][qq];
+          if (q == 0) {
+            acc[i] = t;
+          } else {
+            acc[i].x += t.x;
+            acc[i].y += t.y;
+            acc[i].z += t.z;
+            acc[i].w += t.w;
           }
         }
       }
-#pragma unroll
-      for (int qq = 0; qq < WG; ++qq) {
-        const uint32_t q = q0 + qq;
-        if (q >= W) continue;
-        const float t0 = o.x != ~0u && o.y != ~0u ? a[qq].x + b[qq].x : a[qq].x;
-        const float t1 = o.x != ~0u && o.y != ~0u ? a[qq].y + b[qq].y : a[qq].y;
-        acc0 = q ? acc0 + t0 : t0;
-        acc1 = q ? acc1 + t1 : t1;
-      }
     }
-    dsum[e] = acc0;
-    dsum[e + 1] = acc1;
+#pragma unroll
+    for (int i = 0; i < kQuads; ++i)
+      if (base + i * NTHR + threadIdx.x < nquads) *reinterpret_cast<float4*>(dsum + eq[i]) = acc[i];
   }
   consumers_sync();
 }

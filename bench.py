@@ -447,6 +447,7 @@ def run_ours(args) -> None:
     torch.cuda.set_device(local)
     if world > 1:
         import datetime
+        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep stdout to the one JSON line
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     stack = FFNStack(H, I, device=local, rank=rank, world=world)
