@@ -249,24 +249,45 @@ def _q4_on_gpu(rows: int, cols: int, seed: int, dev):
     return out
 
 
-def extra_configs(device: int) -> dict:
+EXTRA_CASES = ("config1", "config2", "config5", "config3")
+
+
+def extra_configs(device: int, only: str | None = None) -> dict:
     """BASELINE configs 1, 2 and 5 plus the decode-batch sweep, each through
     the library's C ABI on weights rotated over more distinct copies than L2
-    holds (>= 4 x 126 MB), so every call streams its weights from HBM."""
-    import ctypes
-
+    holds (>= 4 x 126 MB), so every call streams its weights from HBM, and
+    config 3 (Llama decode).  `only` runs one of EXTRA_CASES (config5
+    includes the sweep)."""
     import torch
 
-    from alveare_b200 import FusedFFNWeight, Q4Weight, _lib
+    from alveare_b200 import _lib
     dev = torch.device("cuda", device)
     st = torch.cuda.Stream(device=dev)
-    sp = st.cuda_stream
     ctx = _lib.context(device)
-    lib = ctx.lib
     peak = load_peaks()["hbm_gbs"]
     out = {}
 
-    # config 1: gemv 6912 x 1152, fp32 x and y, 128 weight copies (573 MB)
+    def want(case: str) -> bool:
+        return only is None or only == case
+
+    if want("config1"):
+        out.update(_config1(ctx, dev, st, peak))
+    if want("config2"):
+        out.update(_config2(ctx, dev, st, peak))
+    if want("config5"):
+        out.update(_config5(ctx, dev, st, peak))
+    torch.cuda.synchronize(dev)
+    if want("config3"):
+        out["config3_llama32_1b_greedy_decode"] = llama_decode(device)
+    return out
+
+
+def _config1(ctx, dev, st, peak) -> dict:
+    import torch
+
+    from alveare_b200 import Q4Weight, _lib
+    # gemv 6912 x 1152, fp32 x and y, 128 weight copies (573 MB)
+    lib, sp, device, out = ctx.lib, st.cuda_stream, dev.index, {}
     N1, K1, C1 = 6912, 1152, 128
     ws = [Q4Weight(_q4_on_gpu(N1, K1, 10_000 + i, dev), N=N1, K=K1, device=device) for i in range(C1)]
     x = torch.randn(K1, device=dev)
@@ -282,9 +303,15 @@ def extra_configs(device: int) -> dict:
                                      "rotation": f"{C1} weight copies, {C1 * N1 * K1 // 32 * 18 / 1e6:.0f} MB"}
     for w in ws:
         w.free()
-    del ws
+    return out
 
-    # config 2: Gemma-3-1B FFN 1152 x 6912, GeGLU, fp32 x and y, 128 copies (1.72 GB)
+
+def _config2(ctx, dev, st, peak) -> dict:
+    import torch
+
+    from alveare_b200 import FusedFFNWeight, _lib
+    lib, sp, device, out = ctx.lib, st.cuda_stream, dev.index, {}
+    # Gemma-3-1B FFN 1152 x 6912, GeGLU, fp32 x and y, 128 copies (1.72 GB)
     H2, I2, C2 = 1152, 6912, 128
     fs = []
     for i in range(C2):
@@ -304,10 +331,16 @@ def extra_configs(device: int) -> dict:
                                           "rotation": f"{C2} FFN copies, {C2 * b2 / 1e9:.2f} GB"}
     for f in fs:
         f.free()
-    del fs
+    return out
 
-    # config 5: prefill gemm 512 x 3840 x 15360 (tcgen05) and the decode-batch
-    # sweep on the same shape, 8 weight copies (265 MB)
+
+def _config5(ctx, dev, st, peak) -> dict:
+    import torch
+
+    from alveare_b200 import Q4Weight, _lib
+    lib, sp, device, out = ctx.lib, st.cuda_stream, dev.index, {}
+    # prefill gemm 512 x 3840 x 15360 (tcgen05) and the decode-batch sweep on
+    # the same shape, 8 weight copies (265 MB)
     N5, K5, B5, C5 = 15360, 3840, 512, 8
     ws = [Q4Weight(_q4_on_gpu(N5, K5, 30_000 + i, dev), N=N5, K=K5, device=device) for i in range(C5)]
     X = torch.randn((B5, K5), device=dev).to(torch.bfloat16)
@@ -338,9 +371,6 @@ def extra_configs(device: int) -> dict:
     out["decode_batch_sweep_15360x3840"] = sweep
     for w in ws:
         w.free()
-    del ws
-    torch.cuda.synchronize(dev)
-    out["config3_llama32_1b_greedy_decode"] = llama_decode(device)
     return out
 
 
@@ -586,12 +616,18 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the config 1/2/5 measurements")
+    ap.add_argument("--case", choices=EXTRA_CASES, default=None,
+                    help="run only this extra configuration (one GPU; for profiling captures) and print its JSON")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="stack depth (default 48, the benchmark workload; smaller only for profiling captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.case:
+        import torch
+        torch.cuda.set_device(0)
+        print(json.dumps({"case": args.case, **extra_configs(0, args.case)}), flush=True)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
