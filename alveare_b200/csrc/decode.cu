@@ -11,6 +11,7 @@
 // without for prompt tokens) and replayed with no host work per token.
 #include "decode.cuh"
 #include "launch.h"
+#include "llama_step.cuh"
 
 namespace alv {
 namespace {
@@ -42,6 +43,12 @@ struct LlamaModel {
   uint32_t* cnt = nullptr;
   float *ws_gemv = nullptr, *wsA = nullptr, *wsB = nullptr;
   uint8_t* act = nullptr;
+  // one-launch step (llama_step_kernel): per-layer weight table, fp32 down
+  // rows, CTA partials of shared down rows, argmax candidates
+  LlamaLayerW* layers_dev = nullptr;
+  float *down32 = nullptr, *dws = nullptr, *cand_v = nullptr;
+  int* cand_i = nullptr;
+  bool one_launch = false;  // the one-launch step is used (see use_one_launch)
   std::vector<void*> owned;
   cudaGraphExec_t g_prefill = nullptr, g_decode = nullptr;
   bool loaded_emb = false, loaded_rope = false;
@@ -93,6 +100,118 @@ uint32_t proj_rows(const alv_llama_config& c, const std::string& proj) {
 int copy_in(alv_ctx* ctx, void* dst, const void* src, size_t bytes, int on_device) {
   ALV_CUDA(ctx, cudaMemcpy(dst, src, bytes, on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice));
   return ALV_OK;
+}
+
+// The one-launch step needs one dequant path for every matrix (its kernel is
+// compiled per path), head_dim <= 128 (the attention threads hold q, k, v),
+// at most one CTA per query head per SM, and room for its rings.  Otherwise,
+// or when the config asks for it, the step runs as separate kernels.
+// llama_step_kernel's static shared memory beyond the reserve ring_stages
+// keeps (work lists and unit ranges of five matrices per warp).
+constexpr size_t kLlamaStaticSmem = 2048;
+
+size_t llama_other_smem(const LlamaModel* m, uint32_t nctas) {
+  const alv_llama_config& c = m->cfg;
+  const uint32_t kt_max = std::max({m->qkv[0].m.KT, m->o[0].m.KT, m->gu[0].m.KT, m->dn[0].m.KT, m->lm.m.KT});
+  return llama_smem(0, kt_max, c.hidden, c.head_dim, c.max_seq, m->dn[0].m.RT, nctas).end;
+}
+
+int build_one_launch(alv_ctx* ctx, LlamaModel* m) {
+  const alv_llama_config& c = m->cfg;
+  m->one_launch = false;
+  if (c.per_kernel_step == 1) return ALV_OK;
+  const uint32_t fast = m->lm.m.fast;
+  for (int l = 0; l < c.layers; ++l)
+    for (const Mat* mat : {&m->qkv[l], &m->o[l], &m->gu[l], &m->dn[l]})
+      if (mat->m.fast != fast) return ALV_OK;
+  if (c.head_dim > 128 || c.heads > ctx->num_sms) return ALV_OK;
+  const uint32_t nctas = static_cast<uint32_t>(ctx->num_sms);
+  if (!ring_stages(llama_other_smem(m, nctas) + kLlamaStaticSmem)) return ALV_OK;
+  for (const Mat* mat : {&m->qkv[0], &m->o[0], &m->gu[0], &m->dn[0], &m->lm})
+    if (!Partition::fits(mat->m.RT, mat->m.KT)) return ALV_OK;
+  std::vector<LlamaLayerW> lw(c.layers);
+  for (int l = 0; l < c.layers; ++l) {
+    const Mat* mats[4] = {&m->qkv[l], &m->o[l], &m->gu[l], &m->dn[l]};
+    for (int k = 0; k < 4; ++k) {
+      lw[l].mat[k] = mats[k]->m.units;
+      lw[l].mul[k] = mats[k]->m.scale_mul;
+    }
+  }
+  int rc;
+  if ((rc = model_alloc(ctx, m, &m->layers_dev, lw.size() * sizeof(LlamaLayerW))) ||
+      (rc = model_alloc(ctx, m, &m->down32, static_cast<size_t>(c.hidden) * 4)) ||
+      (rc = model_alloc(ctx, m, &m->dws, ws_floats(ctx, 1) * 4)) ||
+      (rc = model_alloc(ctx, m, &m->cand_v, nctas * 4)) || (rc = model_alloc(ctx, m, &m->cand_i, nctas * 4)))
+    return rc;
+  ALV_CUDA(ctx, cudaMemcpy(m->layers_dev, lw.data(), lw.size() * sizeof(LlamaLayerW), cudaMemcpyHostToDevice));
+  m->one_launch = true;
+  return ALV_OK;
+}
+
+template <bool FAST>
+int launch_llama_step_t(alv_ctx* ctx, const LlamaStepParams& p, size_t smem, cudaStream_t st) {
+  auto k = llama_step_kernel<FAST>;
+  // Grid barriers between the phases: every CTA must be resident at once.
+  int rc = prepare_kernel(ctx, k, smem, kThreadsPerCta, ctx->num_sms);
+  if (rc) return rc;
+  return launch_cooperative(ctx, k, p, ctx->num_sms, kThreadsPerCta, smem, st);
+}
+
+// One decode step as one launch of llama_step_kernel.
+int launch_llama_step(alv_ctx* ctx, LlamaModel* m, bool logits, cudaStream_t st) {
+  const alv_llama_config& c = m->cfg;
+  const uint32_t nctas = static_cast<uint32_t>(ctx->num_sms);
+  LlamaStepParams p{};
+  p.layers = m->layers_dev;
+  p.lm = m->lm.m.units;
+  p.lm_mul = m->lm.m.scale_mul;
+  p.L = static_cast<uint32_t>(c.layers);
+  const Mat* mats[kLlamaMats] = {&m->qkv[0], &m->o[0], &m->gu[0], &m->dn[0], &m->lm};
+  for (int k = 0; k < kLlamaMats; ++k) {
+    const Q4Mat& q = mats[k]->m;
+    p.mat[k] = q;
+    // the separate-kernel step's partitions: gemv_kernel (row-aligned when
+    // RT * 4 >= grid) for qkv, o and the LM head; ffn_kernel's for gate/up
+    // (row-aligned) and down
+    const bool aligned = k == 2 ? true : (k == 3 ? false : q.RT * 4 >= nctas);
+    p.pt[k] = Partition::make(q.RT, q.KT, nctas, aligned);
+  }
+  p.H = c.hidden;
+  p.I = c.intermediate;
+  p.nq = c.heads;
+  p.nkv = c.kv_heads;
+  p.hd = c.head_dim;
+  p.max_seq = c.max_seq;
+  p.V = c.vocab;
+  p.eps = c.rms_eps;
+  p.attn_scale = 1.0 / std::sqrt(static_cast<double>(c.head_dim));
+  p.logits = logits ? 1 : 0;
+  p.emb = m->emb;
+  p.norms = m->norms;
+  p.rope = m->rope;
+  p.kcache = m->kcache;
+  p.vcache = m->vcache;
+  p.state = m->state;
+  p.tokens = m->tokens;
+  p.pred = m->pred;
+  p.qkvb = m->qkvb;
+  p.attn = m->attn;
+  p.proj = m->proj;
+  p.logit16 = m->logits;
+  p.act = m->act;
+  p.down = m->down32;
+  p.dws = m->dws;
+  p.fx = Fixup{m->ws_gemv, m->cnt};
+  p.cand_v = m->cand_v;
+  p.cand_i = m->cand_i;
+  p.bar = m->bar;
+  p.status = m->status;
+  p.trace = ctx->trace;
+  const size_t other = llama_other_smem(m, nctas);
+  p.nst = ring_stages(other + kLlamaStaticSmem);
+  if (!p.nst) return fail(ctx, ALV_ERR_UNSUPPORTED, "llama: the one-launch step does not fit in shared memory");
+  const size_t smem = ring_smem_bytes(p.nst) + other;
+  return m->lm.m.fast ? launch_llama_step_t<true>(ctx, p, smem, st) : launch_llama_step_t<false>(ctx, p, smem, st);
 }
 
 // Repack every loaded matrix into the unit layout (once, before the first step).
@@ -156,6 +275,7 @@ int build_model(alv_ctx* ctx, Weight* w, LlamaModel* m) {
   m->wsA = reinterpret_cast<float*>(w->ws + o_a);
   m->wsB = reinterpret_cast<float*>(w->ws + o_b);
   m->act = w->ws + o_act;
+  if ((rc = build_one_launch(ctx, m))) return rc;
   m->built = true;
   return ALV_OK;
 }
@@ -191,6 +311,7 @@ int ffn_into(alv_ctx* ctx, LlamaModel* m, int l, const uint16_t* x, uint16_t* y,
 // One decode step: the token at state.pos through every layer; with
 // `logits`, the LM head and the argmax that writes the next token.
 int enqueue_step(alv_ctx* ctx, LlamaModel* m, bool logits, cudaStream_t st) {
+  if (m->one_launch) return launch_llama_step(ctx, m, logits, st);
   const alv_llama_config& c = m->cfg;
   const int H = c.hidden, L = c.layers;
   const float eps = c.rms_eps;
@@ -495,6 +616,24 @@ extern "C" int alv_llama_forward(alv_ctx* ctx, alv_handle h, int token, int pos,
   if ((rc = enqueue_step(ctx, m, logits != nullptr, st))) return rc;
   if (logits)
     ALV_CUDA(ctx, cudaMemcpyAsync(logits, m->logits, static_cast<size_t>(m->cfg.vocab) * 2, cudaMemcpyDeviceToDevice, st));
+  return ALV_OK;
+}
+
+extern "C" int alv_llama_info(alv_ctx* ctx, alv_handle h, int64_t* info) {
+  if (!ctx || !info) return ALV_ERR_ARG;
+  Weight* w = get_weight(ctx, h, 4);
+  if (!w) return fail(ctx, ALV_ERR_HANDLE, "llama_info: invalid handle (not a llama model)");
+  auto* m = static_cast<LlamaModel*>(w->model);
+  int rc = set_device(ctx);
+  if (rc) return rc;
+  if ((rc = build_model(ctx, w, m))) return rc;
+  size_t bytes = m->lm.bytes;
+  for (int l = 0; l < m->cfg.layers; ++l) bytes += m->qkv[l].bytes + m->o[l].bytes + m->gu[l].bytes + m->dn[l].bytes;
+  info[0] = m->one_launch ? 1 : 0;
+  info[1] = m->one_launch ? 1 : 7 * static_cast<int64_t>(m->cfg.layers) + 3;
+  info[2] = m->cfg.layers;
+  info[3] = static_cast<int64_t>(bytes);
+  for (int i = 4; i < 8; ++i) info[i] = 0;
   return ALV_OK;
 }
 

@@ -167,6 +167,52 @@ __global__ void __launch_bounds__(kDecodeThreads) rope_cache_kernel(const RopePa
   }
 }
 
+// k_j . q for one cached key row (hd bf16 values), fmaf in d order.  The
+// row's 16-byte loads are issued in batches of 8 before the products, so a
+// row costs one memory round trip per 64 values, not one per 8.
+__device__ __forceinline__ float attn_dot(const uint16_t* kr, const float* qs, int hd) {
+  float dot = 0.f;
+  for (int d0 = 0; d0 < hd; d0 += 64) {
+    uint4 kw[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      if (d0 + c * 8 < hd) kw[c] = *reinterpret_cast<const uint4*>(kr + d0 + c * 8);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      if (d0 + c * 8 >= hd) break;
+      const uint32_t ws[4] = {kw[c].x, kw[c].y, kw[c].z, kw[c].w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        dot = fmaf(bf16_bits_to_f32(ws[t] & 0xFFFFu), qs[d0 + c * 8 + 2 * t], dot);
+        dot = fmaf(bf16_bits_to_f32(ws[t] >> 16), qs[d0 + c * 8 + 2 * t + 1], dot);
+      }
+    }
+  }
+  return dot;
+}
+
+// sum over j = g, g + G, ... < seq of p_j v_j[d], fmaf in j order; the
+// cached values are loaded 8 at a time ahead of the products.  j == own
+// (if own >= 0) takes v_own instead of the cache.
+__device__ __forceinline__ float attn_pv(const float* sc, const uint16_t* vb, int hd, int d, int g, int G, int seq,
+                                         int own, float v_own) {
+  float acc = 0.f;
+  for (int j0 = g; j0 < seq; j0 += 8 * G) {
+    float vv[8];
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      const int j = j0 + b * G;
+      vv[b] = j < seq ? (j == own ? v_own : bf16_bits_to_f32(vb[static_cast<size_t>(j) * hd + d])) : 0.f;
+    }
+#pragma unroll
+    for (int b = 0; b < 8; ++b) {
+      const int j = j0 + b * G;
+      if (j < seq) acc = fmaf(sc[j], vv[b], acc);
+    }
+  }
+  return acc;
+}
+
 // GQA attention of one query head per CTA over positions [0, pos]
 // (model.py:580-630): s_j = (k_j . q) * scale (fp32 dot, the scale applied
 // in double like numpy's float64 scalar), softmax with exp(s_j - max)
@@ -198,17 +244,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
   const uint16_t* vb = p.vcache + static_cast<size_t>(kvh) * p.max_seq * p.hd;
   float mx = -INFINITY;
   for (int j = threadIdx.x; j < seq; j += blockDim.x) {
-    const uint16_t* kr = kb + static_cast<size_t>(j) * p.hd;
-    float dot = 0.f;
-    for (int d = 0; d < p.hd; d += 8) {
-      const uint4 w = *reinterpret_cast<const uint4*>(kr + d);
-      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        dot = fmaf(bf16_bits_to_f32(ws[t] & 0xFFFFu), qs[d + 2 * t], dot);
-        dot = fmaf(bf16_bits_to_f32(ws[t] >> 16), qs[d + 2 * t + 1], dot);
-      }
-    }
+    const float dot = attn_dot(kb + static_cast<size_t>(j) * p.hd, qs, p.hd);
     const float s = static_cast<float>(static_cast<double>(dot) * p.scale);
     sc[j] = s;
     mx = fmaxf(mx, s);
@@ -226,11 +262,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
   // out[d] = sum_j p_j v_j[d]: thread (g, d) sums j = g, g+G, ...
   const int G = blockDim.x / p.hd;
   const int g = threadIdx.x / p.hd, d = threadIdx.x - g * p.hd;
-  if (g < G) {
-    float acc = 0.f;
-    for (int j = g; j < seq; j += G) acc = fmaf(sc[j], bf16_bits_to_f32(vb[static_cast<size_t>(j) * p.hd + d]), acc);
-    part[g * p.hd + d] = acc;
-  }
+  if (g < G) part[g * p.hd + d] = attn_pv(sc, vb, p.hd, d, g, G, seq, -1, 0.f);
   __syncthreads();
   for (int e = threadIdx.x; e < p.hd; e += blockDim.x) {
     float o = 0.f;

@@ -38,11 +38,11 @@ class LlamaConfig(ctypes.Structure):
     _fields_ = [("hidden", ctypes.c_int32), ("intermediate", ctypes.c_int32), ("heads", ctypes.c_int32),
                 ("kv_heads", ctypes.c_int32), ("head_dim", ctypes.c_int32), ("layers", ctypes.c_int32),
                 ("vocab", ctypes.c_int32), ("max_seq", ctypes.c_int32), ("rms_eps", ctypes.c_float),
-                ("reserved", ctypes.c_int32 * 7)]
+                ("per_kernel_step", ctypes.c_int32), ("reserved", ctypes.c_int32 * 6)]
 
     @classmethod
-    def llama32_1b(cls, max_seq: int = 2048) -> "LlamaConfig":
-        return cls(2048, 8192, 32, 8, 64, 16, 128256, max_seq, 1e-5)
+    def llama32_1b(cls, max_seq: int = 2048, per_kernel_step: int = 0) -> "LlamaConfig":
+        return cls(2048, 8192, 32, 8, 64, 16, 128256, max_seq, 1e-5, per_kernel_step)
 
 
 def rope_table(head_dim: int, max_seq: int, theta: float = 500000.0) -> np.ndarray:
@@ -183,6 +183,13 @@ class LlamaDecoder:
         self.start(sequence)
         self.run(n_context - 1, len(sequence) - n_context)
         return self.predicted(n_context, len(sequence) - n_context)
+
+    def one_launch(self) -> bool:
+        """Whether a step runs as one kernel launch (else separate kernels);
+        known once the model is built (the first step builds it)."""
+        info = (ctypes.c_int64 * 8)()
+        self.ctx.check(self.ctx.lib.alv_llama_info(self.ctx.ptr, self.handle, info), "alv_llama_info")
+        return bool(info[0])
 
     def free(self) -> None:
         if self.handle:

@@ -230,7 +230,14 @@ int alv_ffn_stack_set_probe(alv_ctx* ctx, alv_handle stack, float* down_last);
 typedef struct {
   int32_t hidden, intermediate, heads, kv_heads, head_dim, layers, vocab, max_seq;
   float rms_eps;        /* 1e-5 for Llama (model.py:532) */
-  int32_t reserved[7];
+  /* 0 (default): a step is one launch of a persistent kernel that runs every
+   * layer, the LM head and the argmax (grid barriers between the phases);
+   * the library falls back to separate kernels when a model does not fit it
+   * (head_dim > 128, more query heads than SMs, mixed dequant paths, or too
+   * little shared memory).  1: always separate kernels (about seven per
+   * layer).  Both give bit-identical logits. */
+  int32_t per_kernel_step;
+  int32_t reserved[6];
 } alv_llama_config;
 
 int alv_llama_create(alv_ctx* ctx, const alv_llama_config* cfg, alv_handle* out);
@@ -284,6 +291,13 @@ int alv_llama_forward(alv_ctx* ctx, alv_handle model, int token, int pos, uint16
 /* Zero the KV cache and the position (runtime/py/model.py reset_caches). */
 int alv_llama_reset(alv_ctx* ctx, alv_handle model, void* stream);
 
+/* info[0..7] = 1 if a step is one kernel launch (0: separate kernels, see
+ * per_kernel_step), kernel launches per step with the LM head, layers,
+ * device bytes of the repacked Q4 weights, 0, 0, 0, 0.  Builds the model
+ * (repacks the loaded tensors) if no step has.  Diagnostics; no counterpart
+ * in the reference. */
+int alv_llama_info(alv_ctx* ctx, alv_handle model, int64_t* info);
+
 /* Allocation-free gemv: same arithmetic and arguments as alv_gemv, for
  * callers that must not allocate device memory while they run (a decode
  * loop with a fixed GPU memory budget, a host runtime that owns the device
@@ -315,7 +329,13 @@ int alv_gemv_noalloc(alv_ctx* ctx, alv_handle h, int ntok, const void* x, int x_
  * normalized x written).  Slots [13]-[15] are unused.  alv_gemv launches
  * write [0] start, [1] weights requested, [2] the previous kernel in the
  * stream finished, [3] x staged, [4] warp 0's units consumed, [5] split-K
- * reduction done.  NULL turns tracing off (the default). */
+ * reduction done.  A one-launch Llama step writes, for its second layer,
+ * [0] layer start, [1] attention norm staged, [2] qkv units consumed (thread
+ * 0's warp), [3] barrier passed, [4] attention done, [5] barrier passed,
+ * [6] attention output staged, [7] O barrier passed, [8] FFN norm staged,
+ * [9] gate/up units consumed, [10] barrier passed, [11] act staged, [12]
+ * down units consumed, [13] barrier passed.  NULL turns tracing off (the
+ * default). */
 int alv_set_trace(alv_ctx* ctx, uint64_t* trace);
 
 /* ---- host-buffer convenience (synchronous, like NpuRegistry::run_gemv) ---- */

@@ -39,9 +39,9 @@ def small_config():
                         vocab_padded=1024, max_seq=64)
 
 
-def decoder_for(cfg, w):
+def decoder_for(cfg, w, per_kernel_step=0):
     c = LlamaConfig(cfg.hidden, cfg.intermediate, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.layers, cfg.vocab,
-                    cfg.max_seq, 1e-5)
+                    cfg.max_seq, 1e-5, per_kernel_step)
     return LlamaDecoder(w, c, device=0, rope_theta=cfg.rope_theta)
 
 
@@ -82,6 +82,31 @@ def test_small_model_forward_and_generate_against_oracle():
     # twice: the graphs are replayed, the cache is reset by generate
     assert dec.generate(prompt, 12) == got
     dec.free()
+
+
+def test_one_launch_step_equals_separate_kernels():
+    """The one-launch step (llama_step_kernel: every layer, the LM head and
+    the argmax in one persistent kernel) computes exactly what the
+    separate-kernel step computes: bit-identical logits at every position
+    and the same greedy tokens.  The small model's projections exercise the
+    unit-balanced partitions (rows split between CTAs) as well as the
+    row-aligned ones."""
+    cfg = small_config()
+    w, _ = llama.synthetic_weights(cfg, seed=11)
+    one = decoder_for(cfg, w)
+    sep = decoder_for(cfg, w, per_kernel_step=1)
+    assert one.one_launch() and not sep.one_launch()
+    stream = [3, 999, 17, 17, 0, 512, 64, 5, 900, 1, 2, 3]
+    one.reset_caches()
+    sep.reset_caches()
+    for pos, tok in enumerate(stream):
+        a = one.forward(tok, pos)
+        b = sep.forward(tok, pos)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), pos
+    prompt = [5, 17, 999, 0, 42]
+    assert one.generate(prompt, 20) == sep.generate(prompt, 20)
+    one.free()
+    sep.free()
 
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "llama_config3.json")
@@ -141,6 +166,13 @@ def test_config3_greedy_tokens_match_reference():
           f"the others are near ties: {[(k, gold['steps'][k]['max'], gold['steps'][k]['second']) for k in miss]}")
     assert all(near_tie(gold["steps"][k]) for k in miss)
     assert len(miss) <= steps // 16
+    # the separate-kernel step predicts exactly the same tokens
+    if dec.one_launch():
+        sep = decoder_for(cfg, llama.synthetic_weights(cfg, seed=gold["seed"], quantize=gpu_quantize)[0],
+                          per_kernel_step=1)
+        assert sep.teacher_forced(gold["prompt"] + ref, len(gold["prompt"])) == forced
+        assert sep.generate(gold["prompt"], steps) == got
+        sep.free()
     dec.free()
 
 
