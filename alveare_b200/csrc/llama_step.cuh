@@ -89,22 +89,39 @@ struct LlamaStepParams {
   unsigned long long* trace;        // optional: phase stamps of layer 1
 };
 
-// Dynamic shared memory after the rings and warp partials.
+// Dynamic shared memory after the rings and warp partials.  The attention
+// area (q, the position's k and v, partial sums, scores, two V chunks)
+// shares its space with the B-fragment area xs: attention runs between the
+// qkv projection, whose fragments are consumed, and the O staging.
 struct LlamaSmem {
-  size_t xs, xres, nw, red, attn, tables, end;
+  size_t xs, attn, xres, nw, red, tables, end;
 };
+__host__ __device__ inline size_t attn_floats(uint32_t hd, uint32_t max_seq) {
+  return (static_cast<size_t>(3 * hd + kAttnThreads + max_seq) + 3) / 4 * 4;
+}
 __host__ __device__ inline LlamaSmem llama_smem(uint32_t nst, uint32_t kt_max, uint32_t H, uint32_t hd,
                                                 uint32_t max_seq, uint32_t dn_rt, uint32_t nctas) {
   LlamaSmem s;
   s.xs = base_smem_bytes(nst, 1);
-  s.xres = s.xs + (frag_bytes(kt_max, 1) + 15) / 16 * 16;
+  s.attn = s.xs;
+  const size_t frag = (frag_bytes(kt_max, 1) + 15) / 16 * 16;
+  const size_t attn = attn_floats(hd, max_seq) * 4 + static_cast<size_t>(2) * kAttnChunk * hd * 2;
+  s.xres = s.xs + (frag > attn ? frag : attn);
   s.nw = s.xres + (static_cast<size_t>(H) * 4 + 15) / 16 * 16;
   s.red = s.nw + (static_cast<size_t>(H) * 4 + 15) / 16 * 16;
-  s.attn = s.red + 64 * 4;
-  s.tables = s.attn + (static_cast<size_t>(3 * hd + kAttnThreads + max_seq) * 4 + 15) / 16 * 16 +
-             static_cast<size_t>(kAttnChunk) * hd * 2;
+  s.tables = s.red + 64 * 4;
   s.end = s.tables + (static_cast<size_t>(dn_rt) * 3 + nctas) * 4;
   return s;
+}
+
+// 16-byte asynchronous copies global -> shared of `n` rows of `hd` bf16
+// (thread t of the 256 attention threads copies vectors t, t + 256, ...).
+__device__ __forceinline__ void attn_copy_rows(uint16_t* dst, const uint16_t* src, uint32_t n, uint32_t hd) {
+  const uint32_t nvec = n * (hd / 8);
+  for (uint32_t e = threadIdx.x; e < nvec; e += kAttnThreads)
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst + 8 * e)), "l"(src + 8 * e)
+                 : "memory");
+  asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
 // Sum of x[h]^2 over h < H in the order of rmsnorm_store on a 1024-thread
@@ -240,14 +257,25 @@ __device__ void llama_attention(const LlamaStepParams& p, uint32_t l, int pos, u
   float* vp = kp + hd;
   float* part = vp + hd;
   float* sc = part + kAttnThreads;
-  // V chunk: after the scores, 16-byte aligned
-  uint16_t* vsh = reinterpret_cast<uint16_t*>(sm + ((3 * hd + kAttnThreads + p.max_seq) + 3) / 4 * 4);
+  // two V chunks of kAttnChunk rows after the scores, 16-byte aligned
+  uint16_t* vbuf = reinterpret_cast<uint16_t*>(sm + attn_floats(hd, p.max_seq));
   const size_t kvl = static_cast<size_t>(p.nkv) * p.max_seq * hd;
   uint16_t* kc = p.kcache + l * kvl + static_cast<size_t>(kvh) * p.max_seq * hd;
   uint16_t* vc = p.vcache + l * kvl + static_cast<size_t>(kvh) * p.max_seq * hd;
   const uint16_t* cs = p.rope + static_cast<size_t>(pos) * 2 * hd;
   const uint32_t t = threadIdx.x;
   const bool writer = head % group == 0;
+  // The cached V rows of the first two chunks start loading now, behind the
+  // RoPE, the scores and the softmax.  (Row `pos` is being written by the
+  // group's first head meanwhile; its copy is never read: v_pos comes from
+  // vp.)
+  const int seq = pos + 1;
+  const int nch = (seq + kAttnChunk - 1) / kAttnChunk;
+  for (int c = 0; c < 2 && c < nch; ++c) {
+    const int c0 = c * kAttnChunk;
+    attn_copy_rows(vbuf + static_cast<size_t>(c & 1) * kAttnChunk * hd, vc + static_cast<size_t>(c0) * hd,
+                   static_cast<uint32_t>(seq - c0 < kAttnChunk ? seq - c0 : kAttnChunk), hd);
+  }
   if (t < half) {
     const uint16_t* q = p.qkvb + head * hd;
     const float x1 = bf16_bits_to_f32(__ldcg(q + t)), x2 = bf16_bits_to_f32(__ldcg(q + t + half));
@@ -274,7 +302,6 @@ __device__ void llama_attention(const LlamaStepParams& p, uint32_t l, int pos, u
     if (writer) vc[static_cast<size_t>(pos) * hd + d] = v;
   }
   attn_sync();
-  const int seq = pos + 1;
   float mx = -INFINITY;
   for (int j = static_cast<int>(t); j < seq; j += kAttnThreads) {
     float dot = 0.f;
@@ -298,24 +325,32 @@ __device__ void llama_attention(const LlamaStepParams& p, uint32_t l, int pos, u
   for (int j = static_cast<int>(t); j < seq; j += kAttnThreads) sc[j] = __fdiv_rn(sc[j], sum);
   attn_sync();
   // out[d] = sum_j p_j v_j[d], thread (g, d) summing j = g, g + G, ... in
-  // order (as attention_kernel); the cached rows come through shared memory
-  // a chunk at a time, every load of a chunk in flight at once.
+  // order (as attention_kernel); the cached rows come through shared memory,
+  // double-buffered: chunk c + 2 loads while chunk c + 1 is summed.
   const uint32_t G = kAttnThreads / hd;
   const uint32_t g = t / hd, d = t - g * hd;
-  const uint32_t row_vecs = hd / 8;
   float acc = 0.f;
-  for (int c0 = 0; c0 < seq; c0 += kAttnChunk) {
-    const int n = seq - c0 < kAttnChunk ? seq - c0 : kAttnChunk;
-    const uint32_t nvec = static_cast<uint32_t>(n) * row_vecs;
-    const uint4* src = reinterpret_cast<const uint4*>(vc + static_cast<size_t>(c0) * hd);
-    for (uint32_t e = t; e < nvec; e += kAttnThreads) reinterpret_cast<uint4*>(vsh)[e] = src[e];
+  for (int c = 0; c < nch; ++c) {
+    if (c + 1 < nch) {
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
     attn_sync();
+    const int c0 = c * kAttnChunk;
+    const int n = seq - c0 < kAttnChunk ? seq - c0 : kAttnChunk;
+    const uint16_t* vsh = vbuf + static_cast<size_t>(c & 1) * kAttnChunk * hd;
     if (g < G)
       for (int j = c0 + static_cast<int>(g); j < c0 + n; j += static_cast<int>(G)) {
         const float v = j == pos ? vp[d] : bf16_bits_to_f32(vsh[static_cast<size_t>(j - c0) * hd + d]);
         acc = fmaf(sc[j], v, acc);
       }
     attn_sync();
+    if (c + 2 < nch) {
+      const int c2 = (c + 2) * kAttnChunk;
+      attn_copy_rows(vbuf + static_cast<size_t>(c & 1) * kAttnChunk * hd, vc + static_cast<size_t>(c2) * hd,
+                     static_cast<uint32_t>(seq - c2 < kAttnChunk ? seq - c2 : kAttnChunk), hd);
+    }
   }
   if (g < G) part[g * hd + d] = acc;
   attn_sync();
@@ -341,7 +376,7 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) llama_step_kernel(const __g
   float* xres = reinterpret_cast<float*>(smem + lay.xres);
   float* nw = reinterpret_cast<float*>(smem + lay.nw);  // the current norm weights
   float* red = reinterpret_cast<float*>(smem + lay.red);
-  float* asm_ = reinterpret_cast<float*>(smem + lay.attn);
+  float* asm_ = reinterpret_cast<float*>(smem + lay.attn);  // (shares xs)
   uint2* split = reinterpret_cast<uint2*>(smem + lay.tables);
   uint32_t* span = reinterpret_cast<uint32_t*>(split + p.mat[3].RT);
   uint32_t* cfirst = span + p.mat[3].RT;
@@ -474,7 +509,12 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) llama_step_kernel(const __g
     trace_mark(tr, 6);
     const RowsEpi eo{nullptr, p.proj, H, H, __ldg(&lw->mul[1])};
     ok = consume_range<1, false, FAST>(ring, p.mat[1], wr[1][warp][0], wr[1][warp][1], xs, fx, 1, eo, p.status);
+    trace_mark(tr, 14);
     cta_fixup(p.pt[1], &wr[1][0][0], fx, 1, eo);
+    if (tr) {
+      consumers_sync();
+      trace_mark(tr, 15);
+    }
     if (!barrier(ok)) break;
     trace_mark(tr, 7);
     // ---- residual + FFN RMSNorm, gate/up with SwiGLU

@@ -252,7 +252,7 @@ def _q4_on_gpu(rows: int, cols: int, seed: int, dev):
 EXTRA_CASES = ("config1", "config2", "config5", "config3")
 
 
-def extra_configs(device: int, only: str | None = None) -> dict:
+def extra_configs(device: int, only: str | None = None, trace: bool = False) -> dict:
     """BASELINE configs 1, 2 and 5 plus the decode-batch sweep, each through
     the library's C ABI on weights rotated over more distinct copies than L2
     holds (>= 4 x 126 MB), so every call streams its weights from HBM, and
@@ -278,7 +278,7 @@ def extra_configs(device: int, only: str | None = None) -> dict:
         out.update(_config5(ctx, dev, st, peak))
     torch.cuda.synchronize(dev)
     if want("config3"):
-        out["config3_llama32_1b_greedy_decode"] = llama_decode(device)
+        out["config3_llama32_1b_greedy_decode"] = llama_decode(device, trace=trace)
     return out
 
 
@@ -374,7 +374,14 @@ def _config5(ctx, dev, st, peak) -> dict:
     return out
 
 
-def llama_decode(device: int, steps: int = 256, n_prompt: int = 128) -> dict:
+LLAMA_PHASES = ((0, "layer start"), (1, "residual + attention norm"), (2, "qkv streamed"),
+                (3, "qkv reduced + grid barrier"), (4, "rope + attention"), (5, "grid barrier after attention"),
+                (6, "attention output staged"), (14, "o streamed"), (15, "o reduced"), (7, "grid barrier after o"),
+                (8, "residual + ffn norm"), (9, "gate/up streamed"), (10, "gate/up reduced + grid barrier"),
+                (11, "act staged"), (12, "down streamed"), (13, "down reduced + grid barrier"))
+
+
+def llama_decode(device: int, steps: int = 256, n_prompt: int = 128, trace: bool = False) -> dict:
     """Llama-3.2-1B shape, random-init Q4 weights (N(0,
     0.02), quantized on the GPU; K/V padding rows zero as on disk), a
     128-token random prompt, then `steps` greedy tokens; tokens/s of the
@@ -407,30 +414,47 @@ def llama_decode(device: int, steps: int = 256, n_prompt: int = 128) -> dict:
             w[f"blk.{l}.{p}.weight_packed"] = q4_quantize_dev(m)
             weight_bytes += real * cols // 32 * 18   # the padding rows are not streamed
             del m
-    dec = LlamaDecoder(w, cfg, device=device)
-    del w
     prompt = torch.randint(0, V, (n_prompt,), generator=torch.Generator().manual_seed(78)).tolist()
     st = torch.cuda.current_stream(dev)
-    for _ in range(2):   # warm-up (graph capture on the first)
+
+    def timed(per_kernel_step: int):
+        cfg.per_kernel_step = per_kernel_step
+        dec = LlamaDecoder(w, cfg, device=device)
+        for _ in range(2):   # warm-up (graph capture on the first)
+            dec.start(prompt)
+            dec.run(n_prompt - 1, 8)
         dec.start(prompt)
-        dec.run(n_prompt - 1, 8)
-    dec.start(prompt)
-    dec.run(n_prompt - 1, 0)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    st.synchronize()
-    e0.record(st)
-    dec.run(0, steps)
-    e1.record(st)
-    st.synchronize()
-    ms = e0.elapsed_time(e1)
-    toks = dec.tokens(n_prompt, steps)
-    dec.free()
-    us = ms * 1e3 / steps
-    return {"us_per_token": round(us, 2), "tokens_per_s": round(steps / ms * 1e3, 1),
+        dec.run(n_prompt - 1, 0)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        st.synchronize()
+        e0.record(st)
+        dec.run(0, steps)
+        e1.record(st)
+        st.synchronize()
+        toks = dec.tokens(n_prompt, steps)
+        one = dec.one_launch()
+        phases = None
+        if trace and one:  # the stamps of layer 1 of one step at position n_prompt + steps / 2
+            ctx = dec.ctx
+            tr = torch.zeros((ctx.info()["num_sms"], 16), dtype=torch.int64, device=dev)
+            ctx.check(ctx.lib.alv_set_trace(ctx.ptr, tr.data_ptr()), "alv_set_trace")
+            dec.forward(toks[steps // 2], n_prompt + steps // 2, return_logits=True)
+            ctx.check(ctx.lib.alv_set_trace(ctx.ptr, None), "alv_set_trace")
+            phases = trace_summary(tr.cpu().numpy().astype("float64"), LLAMA_PHASES)
+        dec.free()
+        return e0.elapsed_time(e1) * 1e3 / steps, toks, one, phases
+
+    us, toks, one, phases = timed(0)
+    us_sep, toks_sep, _, _ = timed(1)
+    del w
+    return {"us_per_token": round(us, 2), "tokens_per_s": round(1e6 / us, 1),
             "q4_bytes_per_token": weight_bytes, "gbs": round(weight_bytes / us / 1e3, 1),
             "frac_of_hbm": round(weight_bytes / us / 1e3 / load_peaks()["hbm_gbs"], 4),
+            "launches_per_token": 1 if one else 7 * cfg.layers + 3,
+            "separate_kernels_us_per_token": round(us_sep, 2), "same_tokens_as_separate_kernels": toks == toks_sep,
             "steps": steps, "prompt": n_prompt, "distinct_tokens": len(set(toks)),
-            "l2": "695 MB of weights per token vs 126 MB L2"}
+            "l2": "695 MB of weights per token vs 126 MB L2",
+            **({"phase_trace_us": phases} if phases else {})}
 
 
 def q4_quantize_dev(w):
@@ -596,6 +620,8 @@ def run_ours(args) -> None:
         "gpu_launches": step_launches * args.steps,
         "clocks": clock_info,
     }
+    if args.trace:
+        line["phase_trace_us"] = stack_phase_trace(stack, rank)
     if rank == 0 and world == 1 and not args.no_extras:
         line["other_configs"] = extra_configs(local)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -608,6 +634,45 @@ def run_ours(args) -> None:
         print(json.dumps(line), flush=True)
 
 
+STACK_PHASES = ((0, "glue start"), (9, "down loaded"), (10, "down norm reduced"), (11, "x norm reduced"),
+                (12, "xn written"), (1, "glue done"), (7, "gate/up streamed"), (2, "gate/up reduced + act"),
+                (3, "grid barrier"), (4, "act staged"), (8, "down streamed"), (5, "down reduced (+ pushed)"),
+                (6, "grid barrier (+ peer exchange)"))
+
+
+def trace_summary(t, phases) -> dict:
+    """Per-phase deltas (us) of the median over CTAs of alv_set_trace stamps."""
+    import numpy as np
+    base = float(np.median(t[:, phases[0][0]]))
+    out, prev = {}, 0.0
+    for i, name in phases:
+        v = (float(np.median(t[:, i])) - base) / 1e3
+        out[name] = round(v - prev, 2)
+        prev = v
+    out["total"] = round(prev, 2)
+    return out
+
+
+def stack_phase_trace(stack, rank: int) -> dict | None:
+    """One more step with rank 0's per-CTA phase stamps on (alv_set_trace;
+    the stack kernel stamps its second layer); every rank runs the step.
+    Returns rank 0's per-phase breakdown of that layer."""
+    import torch
+    ctx = stack.ctx
+    nsm = ctx.info()["num_sms"]
+    tr = torch.zeros((nsm, 16), dtype=torch.int64, device=torch.device("cuda", stack.device))
+    if rank == 0:
+        ctx.check(ctx.lib.alv_set_trace(ctx.ptr, tr.data_ptr()), "alv_set_trace")
+    stack.release()
+    x = torch.zeros(H, dtype=torch.bfloat16).pin_memory()
+    y = torch.empty_like(x).pin_memory()
+    stack.forward(x, y)  # captures a new graph with the trace pointer
+    if rank == 0:
+        ctx.check(ctx.lib.alv_set_trace(ctx.ptr, None), "alv_set_trace")
+        return trace_summary(tr.cpu().numpy().astype("float64"), STACK_PHASES)
+    return None
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -616,6 +681,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true", help="skip the config 1/2/5 measurements")
+    ap.add_argument("--trace", action="store_true",
+                    help="add the per-phase breakdown of one layer (alv_set_trace stamps, rank 0) to the line")
     ap.add_argument("--case", choices=EXTRA_CASES, default=None,
                     help="run only this extra configuration (one GPU; for profiling captures) and print its JSON")
     ap.add_argument("--layers", type=int, default=LAYERS,
@@ -626,7 +693,7 @@ def main():
     if args.case:
         import torch
         torch.cuda.set_device(0)
-        print(json.dumps({"case": args.case, **extra_configs(0, args.case)}), flush=True)
+        print(json.dumps({"case": args.case, **extra_configs(0, args.case, args.trace)}), flush=True)
     elif args.impl == "reference":
         run_reference(args)
     else:

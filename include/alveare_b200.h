@@ -332,7 +332,8 @@ int alv_gemv_noalloc(alv_ctx* ctx, alv_handle h, int ntok, const void* x, int x_
  * reduction done.  A one-launch Llama step writes, for its second layer,
  * [0] layer start, [1] attention norm staged, [2] qkv units consumed (thread
  * 0's warp), [3] barrier passed, [4] attention done, [5] barrier passed,
- * [6] attention output staged, [7] O barrier passed, [8] FFN norm staged,
+ * [6] attention output staged, [14] O units consumed, [15] O reduction done
+ * (all warps), [7] O barrier passed, [8] FFN norm staged,
  * [9] gate/up units consumed, [10] barrier passed, [11] act staged, [12]
  * down units consumed, [13] barrier passed.  NULL turns tracing off (the
  * default). */
