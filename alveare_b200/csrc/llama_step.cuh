@@ -249,8 +249,10 @@ __device__ __forceinline__ float attn_max(float v, float* red) {
 // position's own K and V are used from registers/shared memory (the cache
 // gets them from the group's first head, for later steps), so no barrier
 // separates the append from the reads.
-__device__ void llama_attention(const LlamaStepParams& p, uint32_t l, int pos, uint32_t head, float* sm,
-                                float* red) {
+// Out of line: its own register budget (inlined into the step kernel, whose
+// streaming state stays live around it, its loops spilled).
+static __device__ __noinline__ void llama_attention(const LlamaStepParams& p, uint32_t l, int pos, uint32_t head,
+                                                   float* sm, float* red) {
   const uint32_t hd = p.hd, half = hd / 2, group = p.nq / p.nkv, kvh = head / group;
   float* qs = sm;
   float* kp = qs + hd;
