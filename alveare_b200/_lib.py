@@ -74,6 +74,7 @@ SIGNATURES = {
     "alv_llama_forward": (_i, [_vp, _u32, _i, _i, _vp, _vp]),
     "alv_llama_reset": (_i, [_vp, _u32, _vp]),
     "alv_llama_info": (_i, [_vp, _u32, _vp]),
+    "alv_llama_prefill": (_i, [_vp, _u32, _i, _i, _vp]),
 }
 
 _lock = threading.Lock()

@@ -49,6 +49,9 @@ struct LlamaModel {
   float *down32 = nullptr, *dws = nullptr, *cand_v = nullptr;
   int* cand_i = nullptr;
   bool one_launch = false;  // the one-launch step is used (see use_one_launch)
+  // batched prefill (allocated on first use): rows of kPrefillRows tokens
+  uint16_t *px = nullptr, *pxn = nullptr, *pqkv = nullptr, *pq = nullptr, *pattn = nullptr, *pproj = nullptr,
+           *pgu = nullptr, *pact = nullptr;
   std::vector<void*> owned;
   cudaGraphExec_t g_prefill = nullptr, g_decode = nullptr;
   bool loaded_emb = false, loaded_rope = false;
@@ -308,6 +311,81 @@ int ffn_into(alv_ctx* ctx, LlamaModel* m, int l, const uint16_t* x, uint16_t* y,
   return launch_ffn_params(ctx, p, false, 1, st);
 }
 
+// ---------------------------------------------------------------------------
+// Batched prefill (the reference's run_layer_batch, runtime/cpp/src/model.cpp:
+// 422-571, there gemma4-only with B = 16 padded rows): prompt positions go
+// through each layer kPrefillRows at a time, every projection a tcgen05
+// gemm over the whole batch (the fused gate/up matrix in one gemm, SwiGLU on
+// its interleaved output, the down projection in one gemm: no K split is
+// needed), the glue as the decode step's kernels over rows (one CTA per row;
+// causal attention: row b attends to positions <= pos0 + b, its own K/V
+// appended first).  The roundings are the decode step's; the gemm sums in
+// another order, so the cache and logits agree with the token-by-token path
+// to the last few bf16 bits, not bit for bit.
+// ---------------------------------------------------------------------------
+constexpr int kPrefillRows = 256;
+
+int ensure_prefill(alv_ctx* ctx, LlamaModel* m) {
+  if (m->px) return ALV_OK;
+  const alv_llama_config& c = m->cfg;
+  const size_t R = kPrefillRows, H = c.hidden, nq = static_cast<size_t>(c.heads) * c.head_dim;
+  const size_t nqkv = nq + 2 * static_cast<size_t>(c.kv_heads) * c.head_dim;
+  const size_t ngu = static_cast<size_t>(m->gu[0].m.RT) * 16;
+  int rc;
+  if ((rc = model_alloc(ctx, m, &m->px, R * H * 2)) || (rc = model_alloc(ctx, m, &m->pxn, R * H * 2)) ||
+      (rc = model_alloc(ctx, m, &m->pqkv, R * nqkv * 2)) || (rc = model_alloc(ctx, m, &m->pq, R * nq * 2)) ||
+      (rc = model_alloc(ctx, m, &m->pattn, R * nq * 2)) || (rc = model_alloc(ctx, m, &m->pproj, R * H * 2)) ||
+      (rc = model_alloc(ctx, m, &m->pgu, R * ngu * 2)) ||
+      (rc = model_alloc(ctx, m, &m->pact, R * static_cast<size_t>(c.intermediate) * 2)))
+    return rc;
+  return ALV_OK;
+}
+
+// Positions [pos0, pos0 + n) of tokens[] (n <= kPrefillRows) through every
+// layer: their K/V enter the cache.  No LM head (the last prompt token's
+// logits come from the first decode step).
+int prefill_rows(alv_ctx* ctx, LlamaModel* m, int pos0, int n, cudaStream_t st) {
+  const alv_llama_config& c = m->cfg;
+  const int H = c.hidden, L = c.layers, I = c.intermediate;
+  const uint32_t nq = c.heads * c.head_dim;
+  const float eps = c.rms_eps;
+  const size_t kv_layer = static_cast<size_t>(c.kv_heads) * c.max_seq * c.head_dim;
+  const size_t attn_smem = static_cast<size_t>(c.head_dim + c.max_seq + kAttnThreads) * sizeof(float);
+  int rc = launch_ex(ctx, embed_norm_kernel, dim3(n), dim3(kDecodeThreads), 0, st, false,
+                     static_cast<const uint16_t*>(m->emb), static_cast<const DecodeState*>(nullptr), pos0,
+                     static_cast<const int*>(m->tokens), H, static_cast<const float*>(m->norms), eps, m->px, m->pxn);
+  if (rc) return rc;
+  for (int l = 0; l < L; ++l) {
+    const Mat& q = m->qkv[l];
+    if ((rc = launch_gemm_mat(ctx, q.m, q.rows, q.cols, n, m->pxn, nullptr, m->pqkv, st))) return rc;
+    const RopeParams rp{m->pqkv, m->rope, nullptr, pos0, m->kcache + l * kv_layer, m->vcache + l * kv_layer, m->pq,
+                        c.heads, c.kv_heads, c.head_dim, c.max_seq};
+    if ((rc = launch_ex(ctx, rope_cache_kernel, dim3(n), dim3(kDecodeThreads), 0, st, false, rp))) return rc;
+    const AttnParams ap{m->pq, m->kcache + l * kv_layer, m->vcache + l * kv_layer, nullptr, pos0, m->pattn,
+                        c.heads, c.kv_heads, c.head_dim, c.max_seq, 1.0 / std::sqrt(static_cast<double>(c.head_dim))};
+    if ((rc = launch_ex(ctx, attention_kernel, dim3(c.heads, n), dim3(kAttnThreads), attn_smem, st, false, ap)))
+      return rc;
+    const Mat& o = m->o[l];
+    if ((rc = launch_gemm_mat(ctx, o.m, o.rows, nq, n, m->pattn, nullptr, m->pproj, st))) return rc;
+    if ((rc = launch_ex(ctx, residual_norm_kernel, dim3(n), dim3(kDecodeThreads), 0, st, false, m->px,
+                        static_cast<const uint16_t*>(m->pproj), H,
+                        static_cast<const float*>(m->norms + static_cast<size_t>(2 * l + 1) * H), eps, m->pxn)))
+      return rc;
+    const Mat& gu = m->gu[l];
+    if ((rc = launch_gemm_mat(ctx, gu.m, gu.m.RT * 16, H, n, m->pxn, nullptr, m->pgu, st))) return rc;
+    if ((rc = launch_ex(ctx, swiglu_rows_kernel, dim3((I + 255) / 256, n), dim3(256), 0, st, false,
+                        static_cast<const uint16_t*>(m->pgu), I, m->pact)))
+      return rc;
+    const Mat& dn = m->dn[l];
+    if ((rc = launch_gemm_mat(ctx, dn.m, H, I, n, m->pact, nullptr, m->pproj, st))) return rc;
+    if ((rc = launch_ex(ctx, residual_norm_kernel, dim3(n), dim3(kDecodeThreads), 0, st, false, m->px,
+                        static_cast<const uint16_t*>(m->pproj), H,
+                        static_cast<const float*>(m->norms + static_cast<size_t>(2 * l + 2) * H), eps, m->pxn)))
+      return rc;
+  }
+  return launch_ex(ctx, set_pos_kernel, dim3(1), dim3(32), 0, st, false, m->state, pos0 + n);
+}
+
 // One decode step: the token at state.pos through every layer; with
 // `logits`, the LM head and the argmax that writes the next token.
 int enqueue_step(alv_ctx* ctx, LlamaModel* m, bool logits, cudaStream_t st) {
@@ -316,17 +394,17 @@ int enqueue_step(alv_ctx* ctx, LlamaModel* m, bool logits, cudaStream_t st) {
   const int H = c.hidden, L = c.layers;
   const float eps = c.rms_eps;
   int rc = launch_ex(ctx, embed_norm_kernel, dim3(1), dim3(kDecodeThreads), 0, st, true,
-                     static_cast<const uint16_t*>(m->emb), static_cast<const DecodeState*>(m->state),
+                     static_cast<const uint16_t*>(m->emb), static_cast<const DecodeState*>(m->state), 0,
                      static_cast<const int*>(m->tokens), H, static_cast<const float*>(m->norms), eps, m->x, m->xn);
   if (rc) return rc;
   const size_t kv_layer = static_cast<size_t>(c.kv_heads) * c.max_seq * c.head_dim;
   const size_t attn_smem = static_cast<size_t>(c.head_dim + c.max_seq + kAttnThreads) * sizeof(float);
   for (int l = 0; l < L; ++l) {
     if ((rc = gemv_into(ctx, m, m->qkv[l], m->xn, m->qkvb, st))) return rc;
-    const RopeParams rp{m->qkvb, m->rope, m->state, m->kcache + l * kv_layer, m->vcache + l * kv_layer, m->q,
+    const RopeParams rp{m->qkvb, m->rope, m->state, 0, m->kcache + l * kv_layer, m->vcache + l * kv_layer, m->q,
                         c.heads, c.kv_heads, c.head_dim, c.max_seq};
     if ((rc = launch_ex(ctx, rope_cache_kernel, dim3(1), dim3(kDecodeThreads), 0, st, true, rp))) return rc;
-    const AttnParams ap{m->q, m->kcache + l * kv_layer, m->vcache + l * kv_layer, m->state, m->attn,
+    const AttnParams ap{m->q, m->kcache + l * kv_layer, m->vcache + l * kv_layer, m->state, 0, m->attn,
                         c.heads, c.kv_heads, c.head_dim, c.max_seq, 1.0 / std::sqrt(static_cast<double>(c.head_dim))};
     if ((rc = launch_ex(ctx, attention_kernel, dim3(c.heads), dim3(kAttnThreads), attn_smem, st, true, ap))) return rc;
     if ((rc = gemv_into(ctx, m, m->o[l], m->attn, m->proj, st))) return rc;
@@ -616,6 +694,21 @@ extern "C" int alv_llama_forward(alv_ctx* ctx, alv_handle h, int token, int pos,
   if ((rc = enqueue_step(ctx, m, logits != nullptr, st))) return rc;
   if (logits)
     ALV_CUDA(ctx, cudaMemcpyAsync(logits, m->logits, static_cast<size_t>(m->cfg.vocab) * 2, cudaMemcpyDeviceToDevice, st));
+  return ALV_OK;
+}
+
+extern "C" int alv_llama_prefill(alv_ctx* ctx, alv_handle h, int pos0, int n, void* stream) {
+  if (!ctx || pos0 < 0 || n < 0) return fail(ctx, ALV_ERR_ARG, "llama_prefill: bad argument");
+  Weight* w = get_weight(ctx, h, 4);
+  if (!w) return fail(ctx, ALV_ERR_HANDLE, "llama_prefill: invalid handle (not a llama model)");
+  auto* m = static_cast<LlamaModel*>(w->model);
+  if (pos0 + n > m->cfg.max_seq) return fail(ctx, ALV_ERR_ARG, "llama_prefill: positions beyond max_seq");
+  int rc = set_device(ctx);
+  if (rc) return rc;
+  if ((rc = prepare_model(ctx, w, m)) || (rc = ensure_prefill(ctx, m))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (int p = pos0; p < pos0 + n; p += kPrefillRows)
+    if ((rc = prefill_rows(ctx, m, p, std::min(kPrefillRows, pos0 + n - p), st))) return rc;
   return ALV_OK;
 }
 

@@ -74,16 +74,20 @@ __device__ __forceinline__ void rmsnorm_store(const float (&xv)[PER], int H, con
 constexpr int kDecodePer = 8;  // H <= 8192
 
 // x = bf16(token_embd[tokens[pos]]) (f16 -> bf16, model.py:926);
-// xn = rmsnorm(x) * attn_norm[0].
+// xn = rmsnorm(x) * attn_norm[0].  One CTA per row: with `st` the decode
+// step's position (one row); without it rows b = 0.. of a prefill batch at
+// positions pos0 + b (x and xn (rows, H)).
 __global__ void __launch_bounds__(kDecodeThreads) embed_norm_kernel(const uint16_t* __restrict__ emb,
-                                                                    const DecodeState* st, const int* tokens, int H,
-                                                                    const float* __restrict__ w, float eps,
+                                                                    const DecodeState* st, int pos0, const int* tokens,
+                                                                    int H, const float* __restrict__ w, float eps,
                                                                     uint16_t* __restrict__ x,
                                                                     uint16_t* __restrict__ xn) {
   __shared__ float red[32];
   pdl_wait();
   pdl_trigger();
-  const int tok = tokens[st->pos];
+  x += static_cast<size_t>(blockIdx.x) * H;
+  xn += static_cast<size_t>(blockIdx.x) * H;
+  const int tok = tokens[st ? st->pos : pos0 + static_cast<int>(blockIdx.x)];
   const uint16_t* row = emb + static_cast<size_t>(tok) * H;
   float xv[kDecodePer];
 #pragma unroll
@@ -99,7 +103,8 @@ __global__ void __launch_bounds__(kDecodeThreads) embed_norm_kernel(const uint16
   rmsnorm_store(xv, H, w, eps, xn, red);
 }
 
-// x = bf16(x + add) (model.py:859, 864); xn = rmsnorm(x) * w.
+// x = bf16(x + add) (model.py:859, 864); xn = rmsnorm(x) * w.  One CTA per
+// row (rows of H values).
 __global__ void __launch_bounds__(kDecodeThreads) residual_norm_kernel(uint16_t* __restrict__ x,
                                                                        const uint16_t* __restrict__ add, int H,
                                                                        const float* __restrict__ w, float eps,
@@ -107,6 +112,9 @@ __global__ void __launch_bounds__(kDecodeThreads) residual_norm_kernel(uint16_t*
   __shared__ float red[32];
   pdl_wait();
   pdl_trigger();
+  x += static_cast<size_t>(blockIdx.x) * H;
+  add += static_cast<size_t>(blockIdx.x) * H;
+  xn += static_cast<size_t>(blockIdx.x) * H;
   float xv[kDecodePer];
 #pragma unroll
   for (int i = 0; i < kDecodePer; ++i) {
@@ -128,17 +136,20 @@ __global__ void __launch_bounds__(kDecodeThreads) residual_norm_kernel(uint16_t*
 struct RopeParams {
   const uint16_t* qkv;
   const uint16_t* table;   // [max_seq][2*hd]: cos(hd) then sin(hd)
-  const DecodeState* st;
+  const DecodeState* st;   // the decode step's position; null: prefill rows at pos0 + blockIdx.x
+  int pos0;
   uint16_t* kcache;        // this layer: [nkv][max_seq][hd]
   uint16_t* vcache;
   uint16_t* q_out;         // [nq*hd]
   int nq, nkv, hd, max_seq;
 };
 
-__global__ void __launch_bounds__(kDecodeThreads) rope_cache_kernel(const RopeParams p) {
+__global__ void __launch_bounds__(kDecodeThreads) rope_cache_kernel(RopeParams p) {
   pdl_wait();
   pdl_trigger();
-  const int pos = p.st->pos;
+  const int pos = p.st ? p.st->pos : p.pos0 + static_cast<int>(blockIdx.x);
+  p.qkv += static_cast<size_t>(blockIdx.x) * (p.nq + 2 * p.nkv) * p.hd;
+  p.q_out += static_cast<size_t>(blockIdx.x) * p.nq * p.hd;
   const int half = p.hd / 2;
   const uint16_t* cs = p.table + static_cast<size_t>(pos) * 2 * p.hd;
   const int nq_pairs = p.nq * half, nk_pairs = p.nkv * half;
@@ -222,19 +233,22 @@ struct AttnParams {
   const uint16_t* q;       // [nq*hd] bf16 (after RoPE)
   const uint16_t* kcache;  // this layer
   const uint16_t* vcache;
-  const DecodeState* st;
+  const DecodeState* st;   // the decode step's position; null: prefill rows at pos0 + blockIdx.y
+  int pos0;
   uint16_t* out;           // [nq*hd] bf16
   int nq, nkv, hd, max_seq;
   double scale;
 };
 
-__global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParams p) {
+__global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnParams p) {
   extern __shared__ float sm[];          // [hd] q, [max_seq] scores, [blockDim / hd][hd] partial outputs
   __shared__ float red[32];
   pdl_wait();
   pdl_trigger();
   const int head = blockIdx.x, kvh = head / (p.nq / p.nkv);
-  const int seq = p.st->pos + 1;
+  const int seq = (p.st ? p.st->pos : p.pos0 + static_cast<int>(blockIdx.y)) + 1;  // causal: up to the row's position
+  p.q += static_cast<size_t>(blockIdx.y) * p.nq * p.hd;
+  p.out += static_cast<size_t>(blockIdx.y) * p.nq * p.hd;
   float* qs = sm;
   float* sc = sm + p.hd;
   float* part = sc + p.max_seq;

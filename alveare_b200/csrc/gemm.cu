@@ -2,8 +2,8 @@
 // tensor cores (gemm_tc_kernel).
 #include <cuda.h>
 
-#include "internal.h"
 #include "gemm_tc.cuh"
+#include "launch.h"
 
 using namespace alv;
 
@@ -54,16 +54,15 @@ int launch_gemm_f(alv_ctx* ctx, const GemmParams& p, const CUtensorMap& map, uin
 
 }  // namespace
 
-extern "C" int alv_gemm(alv_ctx* ctx, alv_handle h, int B, const uint16_t* x, void* y, int y_dtype, void* stream) {
-  if (!ctx || !x || !y || B < 1 || !valid_dtype(y_dtype)) return fail(ctx, ALV_ERR_ARG, "gemm: bad argument");
-  Weight* w = get_weight(ctx, h, 1);
-  if (!w) return fail(ctx, ALV_ERR_HANDLE, "gemm: invalid handle (not a gemv weight)");
+// The tcgen05 prefill gemm on a repacked matrix: Y[b, n] = sum_k X[b, k] W[n, k]
+// for b < B, X bf16 (B, K) row-major and 16-byte aligned, Y (B, N) fp32 and/or bf16.
+int alv::launch_gemm_mat(alv_ctx* ctx, const Q4Mat& m, uint32_t N, uint32_t K, int B, const uint16_t* x,
+                         float* y32, uint16_t* y16, cudaStream_t st) {
+  if (B < 1 || !x || (!y32 && !y16)) return fail(ctx, ALV_ERR_ARG, "gemm: bad argument");
   if (reinterpret_cast<uintptr_t>(x) & 15) return fail(ctx, ALV_ERR_ARG, "gemm: x must be 16-byte aligned");
-  int rc = set_device(ctx);
-  if (rc) return rc;
   EncodeTiledFn enc = nullptr;
-  if ((rc = tensor_map_encoder(ctx, &enc))) return rc;
-  const uint32_t K = w->a.cols;
+  int rc = tensor_map_encoder(ctx, &enc);
+  if (rc) return rc;
   const uint32_t nt = B >= 256 ? 256 : (B > 64 ? 128 : 64);
   CUtensorMap map;
   const cuuint64_t dims[2] = {K, static_cast<cuuint64_t>(B)};
@@ -75,12 +74,21 @@ extern "C" int alv_gemm(alv_ctx* ctx, alv_handle h, int B, const uint16_t* x, vo
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (cr != CUDA_SUCCESS) return fail(ctx, ALV_ERR_CUDA, "gemm: cuTensorMapEncodeTiled failed (" + std::to_string(cr) + ")");
   GemmParams p{};
-  p.m = w->a.m;
-  p.N = w->a.rows;
+  p.m = m;
+  p.N = N;
   p.B = static_cast<uint32_t>(B);
-  p.y32 = y_dtype == ALV_F32 ? static_cast<float*>(y) : nullptr;
-  p.y16 = y_dtype == ALV_BF16 ? static_cast<uint16_t*>(y) : nullptr;
+  p.y32 = y32;
+  p.y16 = y16;
   p.status = status_ptr(ctx);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   return p.m.fast ? launch_gemm_f<true>(ctx, p, map, nt, st) : launch_gemm_f<false>(ctx, p, map, nt, st);
+}
+
+extern "C" int alv_gemm(alv_ctx* ctx, alv_handle h, int B, const uint16_t* x, void* y, int y_dtype, void* stream) {
+  if (!ctx || !x || !y || B < 1 || !valid_dtype(y_dtype)) return fail(ctx, ALV_ERR_ARG, "gemm: bad argument");
+  Weight* w = get_weight(ctx, h, 1);
+  if (!w) return fail(ctx, ALV_ERR_HANDLE, "gemm: invalid handle (not a gemv weight)");
+  int rc = set_device(ctx);
+  if (rc) return rc;
+  return launch_gemm_mat(ctx, w->a.m, w->a.rows, w->a.cols, B, x, y_dtype == ALV_F32 ? static_cast<float*>(y) : nullptr,
+                         y_dtype == ALV_BF16 ? static_cast<uint16_t*>(y) : nullptr, static_cast<cudaStream_t>(stream));
 }

@@ -18,6 +18,12 @@ int launch_gemv_params(alv_ctx* ctx, const GemvParams& p, bool split, uint32_t n
 // two).  Defined in ffn.cu.
 int launch_ffn_params(alv_ctx* ctx, const FfnParams& p, bool split, uint32_t nt, cudaStream_t st);
 
+// tcgen05 prefill gemm on a repacked matrix: Y[b, n] = sum_k X[b, k] W[n, k],
+// X bf16 (B, K) row-major, 16-byte aligned; Y (B, N) fp32 and/or bf16 (either
+// may be null).  Defined in gemm.cu.
+int launch_gemm_mat(alv_ctx* ctx, const Q4Mat& m, uint32_t N, uint32_t K, int B, const uint16_t* x, float* y32,
+                    uint16_t* y16, cudaStream_t st);
+
 // Repack a reference-layout (rows, K/32*20) Q4 matrix already on the device
 // into a new unit-layout matrix (its own dequant path).  Defined in core.cu.
 int repack_rows(alv_ctx* ctx, const uint8_t* src, uint32_t rows, uint32_t K, Mat* out);

@@ -22,6 +22,26 @@
 
 namespace alv {
 
+// Batched prefill: act[b][i] = bf16(swiglu(gate, up)) from the gate/up
+// projection of the interleaved matrix (rows 16r..16r+7 gate, 16r+8..16r+15
+// up of intermediate indices 8r..8r+7), gate and up bf16 as the FFN's
+// epilogue rounds them (model.py:689-698 for SwiGLU).
+__global__ void __launch_bounds__(256) swiglu_rows_kernel(const uint16_t* __restrict__ gu, int I,
+                                                          uint16_t* __restrict__ act) {
+  const int b = blockIdx.y;
+  const uint16_t* row = gu + static_cast<size_t>(b) * 2 * I;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < I; i += gridDim.x * blockDim.x) {
+    const int r = i >> 3, g = i & 7;
+    const float gate = bf16_bits_to_f32(row[r * 16 + g]), up = bf16_bits_to_f32(row[r * 16 + 8 + g]);
+    act[static_cast<size_t>(b) * I + i] = bf16_bits_rn(swiglu_ref(gate, up));
+  }
+}
+
+// The position the next decode step consumes, after a batched prefill.
+__global__ void set_pos_kernel(DecodeState* st, int pos) {
+  if (threadIdx.x == 0) st->pos = pos;
+}
+
 // Per-layer weights: 0 [q|k|v], 1 o, 2 gate/up (interleaved), 3 down.
 struct LlamaLayerW {
   const uint8_t* mat[4];

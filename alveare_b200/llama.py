@@ -141,9 +141,16 @@ class LlamaDecoder:
         self.ctx.sync_status(st)
         return (bits.astype(np.uint32) << 16).view(np.float32)
 
-    def generate(self, prompt_ids, max_new_tokens: int) -> list[int]:
-        """Greedy decode: the prompt token by token, then `max_new_tokens`
-        argmax tokens (tests/test_generation.py:72-99 without an EOS stop)."""
+    def generate(self, prompt_ids, max_new_tokens: int, batch_prefill: bool = False) -> list[int]:
+        """Greedy decode: the prompt token by token (or, with batch_prefill,
+        all but its last token in batched prefill: tcgen05 gemms over up to 256
+        positions at a time), then `max_new_tokens` argmax tokens
+        (tests/test_generation.py:72-99 without an EOS stop)."""
+        if batch_prefill:
+            self.start(prompt_ids)
+            self.prefill(0, len(prompt_ids) - 1)
+            self.run(0, max_new_tokens)
+            return self.tokens(len(prompt_ids), max_new_tokens)
         p = np.ascontiguousarray(np.asarray(prompt_ids, dtype=np.int32))
         out = np.empty(max_new_tokens, dtype=np.int32)
         self.ctx.check(self.ctx.lib.alv_llama_generate(self.ctx.ptr, self.handle, p.ctypes.data, len(p),
@@ -157,6 +164,13 @@ class LlamaDecoder:
         self._n_prompt = len(p)
         self.ctx.check(self.ctx.lib.alv_llama_start(self.ctx.ptr, self.handle, p.ctypes.data, len(p), self._stream()),
                        "alv_llama_start")
+
+    def prefill(self, pos0: int, n: int) -> None:
+        """Positions [pos0, pos0 + n) of the started sequence through every
+        layer in batches (the reference's run_layer_batch, model.cpp:422-571);
+        the next step consumes position pos0 + n."""
+        self.ctx.check(self.ctx.lib.alv_llama_prefill(self.ctx.ptr, self.handle, pos0, n, self._stream()),
+                       "alv_llama_prefill")
 
     def run(self, prompt_steps: int, decode_steps: int) -> None:
         self.ctx.check(self.ctx.lib.alv_llama_run(self.ctx.ptr, self.handle, prompt_steps, decode_steps,

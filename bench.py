@@ -431,8 +431,19 @@ def llama_decode(device: int, steps: int = 256, n_prompt: int = 128, trace: bool
         dec.run(0, steps)
         e1.record(st)
         st.synchronize()
+        us_tok = e0.elapsed_time(e1) * 1e3 / steps
         toks = dec.tokens(n_prompt, steps)
         one = dec.one_launch()
+        # batched prefill of the prompt's first n_prompt - 1 positions
+        dec.start(prompt)
+        dec.prefill(0, n_prompt - 1)
+        dec.start(prompt)
+        st.synchronize()
+        e0.record(st)
+        dec.prefill(0, n_prompt - 1)
+        e1.record(st)
+        st.synchronize()
+        prefill_ms = e0.elapsed_time(e1)
         phases = None
         if trace and one:  # the stamps of layer 1 of one step at position n_prompt + steps / 2
             ctx = dec.ctx
@@ -442,16 +453,17 @@ def llama_decode(device: int, steps: int = 256, n_prompt: int = 128, trace: bool
             ctx.check(ctx.lib.alv_set_trace(ctx.ptr, None), "alv_set_trace")
             phases = trace_summary(tr.cpu().numpy().astype("float64"), LLAMA_PHASES)
         dec.free()
-        return e0.elapsed_time(e1) * 1e3 / steps, toks, one, phases
+        return us_tok, toks, one, phases, prefill_ms
 
-    us, toks, one, phases = timed(0)
-    us_sep, toks_sep, _, _ = timed(1)
+    us, toks, one, phases, prefill_ms = timed(0)
+    us_sep, toks_sep, _, _, _ = timed(1)
     del w
     return {"us_per_token": round(us, 2), "tokens_per_s": round(1e6 / us, 1),
             "q4_bytes_per_token": weight_bytes, "gbs": round(weight_bytes / us / 1e3, 1),
             "frac_of_hbm": round(weight_bytes / us / 1e3 / load_peaks()["hbm_gbs"], 4),
             "launches_per_token": 1 if one else 7 * cfg.layers + 3,
             "separate_kernels_us_per_token": round(us_sep, 2), "same_tokens_as_separate_kernels": toks == toks_sep,
+            "batched_prefill_ms": round(prefill_ms, 3), "batched_prefill_tokens_per_s": round((n_prompt - 1) / prefill_ms * 1e3, 1),
             "steps": steps, "prompt": n_prompt, "distinct_tokens": len(set(toks)),
             "l2": "695 MB of weights per token vs 126 MB L2",
             **({"phase_trace_us": phases} if phases else {})}

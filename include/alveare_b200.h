@@ -288,6 +288,16 @@ int alv_llama_generate(alv_ctx* ctx, alv_handle model, const int32_t* prompt, in
  * (model.py:919-934 forward(token, pos)). */
 int alv_llama_forward(alv_ctx* ctx, alv_handle model, int token, int pos, uint16_t* logits, void* stream);
 
+/* Batched prefill (Model::run_layer_batch, runtime/cpp/src/model.cpp:422-571):
+ * positions [pos0, pos0 + n) of the token list alv_llama_start set go
+ * through every layer 256 at a time, each projection one tcgen05 gemm over
+ * the batch and causal attention per row; their K/V enter the cache and the
+ * position becomes pos0 + n.  No LM head: after a prompt of n_prompt tokens,
+ * prefill(0, n_prompt - 1) then run(0, steps) is the greedy loop.  The gemm
+ * sums in another order than the decode step's gemv, so the cache agrees
+ * with the token-by-token path to the last few bf16 bits. */
+int alv_llama_prefill(alv_ctx* ctx, alv_handle model, int pos0, int n, void* stream);
+
 /* Zero the KV cache and the position (runtime/py/model.py reset_caches). */
 int alv_llama_reset(alv_ctx* ctx, alv_handle model, void* stream);
 

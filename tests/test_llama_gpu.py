@@ -109,6 +109,37 @@ def test_one_launch_step_equals_separate_kernels():
     sep.free()
 
 
+def test_batched_prefill_matches_token_by_token():
+    """Batched prefill (tcgen05 gemms over the prompt rows, causal attention
+    per row) fills the KV cache as the token-by-token path does: the logits
+    of the step after the prompt agree normwise (the gemm sums in another
+    order than the gemv, so bf16 values differ in their last bits), the
+    greedy continuation follows the oracle's, and a prompt longer than one
+    batch of 256 rows is handled in pieces."""
+    cfg = small_config()
+    cfg.max_seq = 600
+    w, _ = llama.synthetic_weights(cfg, seed=4)
+    dec = decoder_for(cfg, w)
+    rng = np.random.default_rng(9)
+    for n_prompt in (9, 300):
+        prompt = [int(t) for t in rng.integers(0, cfg.vocab, n_prompt)]
+        dec.start(prompt)
+        dec.run(n_prompt - 1, 0)
+        ref = dec.forward(prompt[-1], n_prompt - 1)
+        dec.start(prompt)
+        dec.prefill(0, n_prompt - 1)
+        got = dec.forward(prompt[-1], n_prompt - 1)
+        assert normwise(got, ref) <= LOGIT_TOL, n_prompt
+        assert int(np.argmax(got)) == int(np.argmax(ref))
+    prompt = [5, 17, 999, 0, 42, 7, 7, 300]
+    orc = llama.LlamaOracle(cfg, w)
+    ref_toks = orc.generate(prompt, 12)
+    got = dec.generate(prompt, 12, batch_prefill=True)
+    agree = next((k for k, (a, b) in enumerate(zip(got, ref_toks)) if a != b), len(got))
+    assert agree >= 8, (got, ref_toks)
+    dec.free()
+
+
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "llama_config3.json")
 
 
@@ -166,6 +197,12 @@ def test_config3_greedy_tokens_match_reference():
           f"the others are near ties: {[(k, gold['steps'][k]['max'], gold['steps'][k]['second']) for k in miss]}")
     assert all(near_tie(gold["steps"][k]) for k in miss)
     assert len(miss) <= steps // 16
+    # batched prefill of the prompt: the same criterion as free-running
+    got_b = dec.generate(gold["prompt"], steps, batch_prefill=True)
+    agree_b = next((k for k, (a, b) in enumerate(zip(got_b, ref)) if a != b), steps)
+    print(f"config 3: with batched prefill, greedy tokens equal the reference's for {agree_b} of {steps} steps")
+    if agree_b < steps:
+        assert near_tie(gold["steps"][agree_b]), gold["steps"][agree_b]
     # the separate-kernel step predicts exactly the same tokens
     if dec.one_launch():
         sep = decoder_for(cfg, llama.synthetic_weights(cfg, seed=gold["seed"], quantize=gpu_quantize)[0],
