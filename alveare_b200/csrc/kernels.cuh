@@ -930,6 +930,54 @@ inline __device__ void push_down(const StackParams& p, uint32_t par, uint32_t ro
   }
 }
 
+// Tensor parallelism with a row-aligned down partition (every down row whole
+// in one CTA, so a rank's slot holds whole rows only): dsum[e] = the ranks'
+// values of element e summed in rank order, as tp_gather computes it, but
+// with one 16-byte load per rank and group of four elements, and the loads
+// of four ranks for two groups per thread in flight together.
+__device__ __forceinline__ void tp_gather_rows(const StackParams& p, uint32_t par, float* dsum) {
+  constexpr uint32_t NTHR = kConsumerWarps * 32;
+  constexpr int WG = 4;      // ranks per batch
+  constexpr int kQuads = 2;  // element quads per thread per pass
+  const uint32_t W = p.world, nquads = static_cast<uint32_t>(p.ntok) * p.H / 4;
+  for (uint32_t base = 0; base < nquads; base += NTHR * kQuads) {
+    float4 acc[kQuads];
+    for (uint32_t q0 = 0; q0 < W; q0 += WG) {
+      float4 a[kQuads][WG];
+#pragma unroll
+      for (int i = 0; i < kQuads; ++i)
+#pragma unroll
+        for (int qq = 0; qq < WG; ++qq) {
+          const uint32_t quad = base + i * NTHR + threadIdx.x;
+          a[i][qq] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (q0 + qq < W && quad < nquads)
+            a[i][qq] = __ldcg(reinterpret_cast<const float4*>(xslot_ptr(p, p.rank, par, q0 + qq) + 4 * quad));
+        }
+#pragma unroll
+      for (int i = 0; i < kQuads; ++i)
+#pragma unroll
+        for (int qq = 0; qq < WG; ++qq) {
+          const uint32_t q = q0 + qq;
+          if (q >= W) continue;
+          if (q == 0) {
+            acc[i] = a[i][qq];
+          } else {
+            acc[i].x += a[i][qq].x;
+            acc[i].y += a[i][qq].y;
+            acc[i].z += a[i][qq].z;
+            acc[i].w += a[i][qq].w;
+          }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < kQuads; ++i) {
+      const uint32_t quad = base + i * NTHR + threadIdx.x;
+      if (quad < nquads) *reinterpret_cast<float4*>(dsum + 4 * quad) = acc[i];
+    }
+  }
+  consumers_sync();
+}
+
 // Tensor parallelism: sum the ranks' partial down projections of the
 // previous layer (their slots in this GPU's exchange region, complete after
 // the peer barrier) into dsum (fp32 [ntok][H], before the glue's bf16
@@ -941,6 +989,10 @@ inline __device__ void push_down(const StackParams& p, uint32_t par, uint32_t ro
 // adds anything (more in flight makes the kernel spill around the call).
 static __device__ __noinline__ void tp_gather(const StackParams& p, uint32_t par, const uint2* split,
                                        const uint32_t* cfirst, const uint32_t* span, float* dsum) {
+  if (p.ptB.aligned) {  // whole rows only: one load per rank and element
+    tp_gather_rows(p, par, dsum);
+    return;
+  }
   constexpr uint32_t NTHR = kConsumerWarps * 32;
   constexpr int WG = 2;      // ranks per batch
   constexpr int kQuads = 1;  // element quads per thread per pass

@@ -16,7 +16,10 @@ int launch_stack_t(alv_ctx* ctx, StackParams p, cudaStream_t st) {
   if (!Partition::fits(p.gu.RT, p.gu.KT) || !Partition::fits(p.dn.RT, p.dn.KT))
     return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn_stack: matrix too large for one launch's partition");
   p.ptA = Partition::make(p.gu.RT, p.gu.KT, nctas, true);
-  p.ptB = Partition::make(p.dn.RT, p.dn.KT, nctas);
+  // Tensor parallelism: whole down rows per CTA, so each rank pushes exactly
+  // its H values per token and the gather reads one value per rank (the
+  // imbalance of whole rows costs less than the partials' exchange).
+  p.ptB = Partition::make(p.dn.RT, p.dn.KT, nctas, TP);
   const size_t other = stack_smem_bytes(0, p.gu.KT, p.dn.KT, NT, p.H, p.ntok, p.dn.RT, nctas);
   p.nst = ring_stages(other);
   if (!p.nst) return fail(ctx, ALV_ERR_UNSUPPORTED, "ffn_stack: H, I or ntok too large for shared memory");
