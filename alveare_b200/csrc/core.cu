@@ -20,7 +20,7 @@ __global__ void activation_kernel(int fn, uint32_t n, const uint16_t* __restrict
   out[i] = bf16_bits_rn(fn == 0 ? geglu_act(g, u) : swiglu_ref(g, u));
 }
 
-// Final residual of an FFN stack: one CTA of 480 threads (the glue's thread
+// Final residual of an FFN stack: one CTA of the consumer threads (the glue's thread
 // layout, so the sums match the in-kernel glue bit for bit).
 __global__ void __launch_bounds__(kConsumerWarps * 32, 1)
     ffn_stack_finalize_kernel(int ntok, uint32_t H, const uint16_t* x_in, const float* down_in, uint16_t* x_out,

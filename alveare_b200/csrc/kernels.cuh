@@ -408,10 +408,11 @@ __device__ __forceinline__ void trace_mark(unsigned long long* trace, int i) {
 //   x  = bf16(x_in + bf16(rmsnorm(bf16(d))))   when a down vector d is given
 //   xn = bf16(rmsnorm(x))                       when PRE
 // with unit-weight rmsnorm v / sqrt(mean(v*v) + eps), the mean dividing the
-// float32 sum by H like np.mean.  Consumer thread t owns h = t + i*480
-// (i < GR) and holds them in registers, so every load of a token is in
-// flight at once; sums are reduced in a fixed order, so every caller and
-// every CTA computes identical values.  H <= 480 * GR.
+// float32 sum by H like np.mean.  Consumer thread t owns the groups of eight
+// consecutive values g = t + k * T (T consumer threads, k < GK) and holds
+// them in registers, so every load of a token is in flight at once; sums are
+// reduced in a fixed order, so every caller and every CTA computes identical
+// values.  H <= 8 * T * GK.
 // ---------------------------------------------------------------------------
 constexpr int kGlueRegs = 16;
 constexpr int kMaxRanks = 8;  // tensor-parallel ranks of one FFN stack

@@ -147,7 +147,7 @@ __device__ __forceinline__ void attn_copy_rows(uint16_t* dst, const uint16_t* sr
 // Sum of x[h]^2 over h < H in the order of rmsnorm_store on a 1024-thread
 // CTA: virtual thread t sums h = t, t + 1024, ... in sequence; a warp's 32
 // virtual threads by the xor tree; the 32 virtual warps in order.  Real
-// warp w plays virtual warps w, w + 15, w + 30.
+// warp w plays virtual warps w, w + W, w + 2W (W consumer warps).
 __device__ __forceinline__ float llama_sumsq(const float* x, uint32_t H, float* red) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int vw = warp; vw < 32; vw += kConsumerWarps) {
@@ -201,7 +201,7 @@ __device__ __forceinline__ void llama_norm_frag(const float* x, uint32_t H, cons
 // every load in flight before the adds: x = bf16(x + v).
 __device__ __forceinline__ void llama_add_bf16(float* x, const uint16_t* v, uint32_t H) {
   constexpr uint32_t NTHR = kConsumerWarps * 32;
-  constexpr int kPairs = 4;  // pairs per thread per pass: one pass for hidden <= 3840
+  constexpr int kPairs = 4;  // pairs per thread per pass: one pass for hidden <= 4096 with 16 warps
   for (uint32_t k0 = 2 * threadIdx.x; k0 < H; k0 += 2 * NTHR * kPairs) {
     uint32_t w[kPairs];
 #pragma unroll
@@ -474,7 +474,7 @@ __global__ void __launch_bounds__(kThreadsPerCta, 1) llama_step_kernel(const __g
   };
   // x += the previous layer's down projection (bf16, as the FFN writes it);
   // a thread's groups of 8 are loaded two at a time before they are added
-  // (one pass for hidden <= 7680).
+  // (one pass for hidden <= 8192 with 16 warps).
   auto add_down = [&](uint32_t l) {
     DownIn d = din;
     d.sm = __ldg(&p.layers[l].mul[3]);

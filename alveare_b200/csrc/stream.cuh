@@ -47,7 +47,7 @@ constexpr int kTileCols = 64;
 
 // Warps per CTA (one CTA per SM), each streaming its own unit range.
 #ifndef ALV_WARPS
-#define ALV_WARPS 15
+#define ALV_WARPS 16
 #endif
 constexpr int kConsumerWarps = ALV_WARPS;
 constexpr uint32_t kWarpsPerCtaS = kConsumerWarps;
