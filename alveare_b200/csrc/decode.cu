@@ -35,6 +35,10 @@ struct LlamaModel {
   uint16_t *x = nullptr, *xn = nullptr, *qkvb = nullptr, *q = nullptr, *attn = nullptr, *proj = nullptr,
            *logits = nullptr;
   DecodeState* state = nullptr;
+  // Host copy of state->pos (every step consumes one position), so that no
+  // run enqueues a step at a position >= max_seq: the device kernels index
+  // the KV cache and the RoPE table with the position unchecked.
+  int64_t next_pos = 0;
   int* tokens = nullptr;       // [max_seq + 1] token at each position
   int* pred = nullptr;         // [max_seq + 1] the argmax each logits step predicted for the next position
   // workspace (Weight::ws): [sync block: status, grid barrier, counters][split-K partials][FFN act]
@@ -450,6 +454,7 @@ int start_sequence(alv_ctx* ctx, LlamaModel* m, const int32_t* prompt, int n, cu
   const DecodeState s{0, n, {0, 0}};
   ALV_CUDA(ctx, cudaMemcpyAsync(m->state, &s, sizeof(s), cudaMemcpyHostToDevice, st));
   ALV_CUDA(ctx, cudaStreamSynchronize(st));  // the host copies above read stack / caller memory
+  m->next_pos = 0;
   return ALV_OK;
 }
 
@@ -462,6 +467,7 @@ int prepare_model(alv_ctx* ctx, Weight* w, LlamaModel* m) {
   const int32_t zero = 0;
   if ((rc = start_sequence(ctx, m, &zero, 1, ctx->stream))) return rc;
   if ((rc = enqueue_step(ctx, m, true, ctx->stream))) return rc;
+  m->next_pos = 1;
   if ((rc = check_status(ctx, ctx->stream))) return rc;
   if ((rc = capture_step(ctx, m, false, &m->g_prefill))) return rc;
   return capture_step(ctx, m, true, &m->g_decode);
@@ -633,9 +639,12 @@ extern "C" int alv_llama_run(alv_ctx* ctx, alv_handle h, int n_prompt_steps, int
   int rc = set_device(ctx);
   if (rc) return rc;
   if ((rc = prepare_model(ctx, w, m))) return rc;
+  if (m->next_pos + n_prompt_steps + n_decode_steps > m->cfg.max_seq)
+    return fail(ctx, ALV_ERR_ARG, "llama_run: the steps would consume positions beyond max_seq (next position " +
+                                      std::to_string(m->next_pos) + ")");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  for (int i = 0; i < n_prompt_steps; ++i) ALV_CUDA(ctx, cudaGraphLaunch(m->g_prefill, st));
-  for (int i = 0; i < n_decode_steps; ++i) ALV_CUDA(ctx, cudaGraphLaunch(m->g_decode, st));
+  for (int i = 0; i < n_prompt_steps; ++i, ++m->next_pos) ALV_CUDA(ctx, cudaGraphLaunch(m->g_prefill, st));
+  for (int i = 0; i < n_decode_steps; ++i, ++m->next_pos) ALV_CUDA(ctx, cudaGraphLaunch(m->g_decode, st));
   return ALV_OK;
 }
 
@@ -644,7 +653,8 @@ int copy_ids(alv_ctx* ctx, alv_handle h, bool predicted, int first, int n, int32
   if (!ctx || !out_host || first < 0 || n < 0) return fail(ctx, ALV_ERR_ARG, "llama_tokens: bad argument");
   LlamaModel* m = get_model(ctx, h);
   if (!m) return fail(ctx, ALV_ERR_HANDLE, "llama_tokens: invalid handle (not a llama model)");
-  if (first + n > m->cfg.max_seq + 1) return fail(ctx, ALV_ERR_ARG, "llama_tokens: range beyond max_seq");
+  if (static_cast<int64_t>(first) + n > static_cast<int64_t>(m->cfg.max_seq) + 1)
+    return fail(ctx, ALV_ERR_ARG, "llama_tokens: range beyond max_seq");
   int rc = set_device(ctx);
   if (rc) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -667,7 +677,7 @@ extern "C" int alv_llama_generate(alv_ctx* ctx, alv_handle h, const int32_t* pro
   if (!ctx || !prompt || !out_host || steps < 0) return fail(ctx, ALV_ERR_ARG, "llama_generate: bad argument");
   LlamaModel* m = get_model(ctx, h);
   if (!m) return fail(ctx, ALV_ERR_HANDLE, "llama_generate: invalid handle (not a llama model)");
-  if (n_prompt < 1 || n_prompt + steps > m->cfg.max_seq)
+  if (n_prompt < 1 || static_cast<int64_t>(n_prompt) + steps > m->cfg.max_seq)
     return fail(ctx, ALV_ERR_ARG, "llama_generate: n_prompt + steps must be <= max_seq (the last step reads position "
                                   "n_prompt + steps - 1)");
   int rc;
@@ -692,6 +702,7 @@ extern "C" int alv_llama_forward(alv_ctx* ctx, alv_handle h, int token, int pos,
   ALV_CUDA(ctx, cudaMemcpyAsync(m->state, &s, sizeof(s), cudaMemcpyHostToDevice, st));
   ALV_CUDA(ctx, cudaStreamSynchronize(st));
   if ((rc = enqueue_step(ctx, m, logits != nullptr, st))) return rc;
+  m->next_pos = static_cast<int64_t>(pos) + 1;
   if (logits)
     ALV_CUDA(ctx, cudaMemcpyAsync(logits, m->logits, static_cast<size_t>(m->cfg.vocab) * 2, cudaMemcpyDeviceToDevice, st));
   return ALV_OK;
@@ -702,13 +713,15 @@ extern "C" int alv_llama_prefill(alv_ctx* ctx, alv_handle h, int pos0, int n, vo
   Weight* w = get_weight(ctx, h, 4);
   if (!w) return fail(ctx, ALV_ERR_HANDLE, "llama_prefill: invalid handle (not a llama model)");
   auto* m = static_cast<LlamaModel*>(w->model);
-  if (pos0 + n > m->cfg.max_seq) return fail(ctx, ALV_ERR_ARG, "llama_prefill: positions beyond max_seq");
+  if (static_cast<int64_t>(pos0) + n > m->cfg.max_seq)
+    return fail(ctx, ALV_ERR_ARG, "llama_prefill: positions beyond max_seq");
   int rc = set_device(ctx);
   if (rc) return rc;
   if ((rc = prepare_model(ctx, w, m)) || (rc = ensure_prefill(ctx, m))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   for (int p = pos0; p < pos0 + n; p += kPrefillRows)
     if ((rc = prefill_rows(ctx, m, p, std::min(kPrefillRows, pos0 + n - p), st))) return rc;
+  m->next_pos = pos0 + n;
   return ALV_OK;
 }
 
@@ -740,5 +753,6 @@ extern "C" int alv_llama_reset(alv_ctx* ctx, alv_handle h, void* stream) {
   ALV_CUDA(ctx, cudaMemsetAsync(m->kcache, 0, m->kv_elems() * 2, st));
   ALV_CUDA(ctx, cudaMemsetAsync(m->vcache, 0, m->kv_elems() * 2, st));
   ALV_CUDA(ctx, cudaMemsetAsync(m->state, 0, sizeof(DecodeState), st));
+  m->next_pos = 0;
   return ALV_OK;
 }

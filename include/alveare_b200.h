@@ -264,6 +264,9 @@ int alv_llama_start(alv_ctx* ctx, alv_handle model, const int32_t* prompt, int n
 /* Enqueue n_prompt_steps steps without logits (prompt tokens), then
  * n_decode_steps steps with logits (LM head + argmax: the argmax becomes the
  * next position's token unless the prompt already holds one there).
+ * Each step consumes one position; ALV_ERR_ARG, before any launch, when the
+ * steps would reach position max_seq (the library tracks the position that
+ * start, prefill, forward, reset and run leave on the host).
  * Asynchronous, stream-ordered. */
 int alv_llama_run(alv_ctx* ctx, alv_handle model, int n_prompt_steps, int n_decode_steps, void* stream);
 

@@ -81,6 +81,22 @@ def test_small_model_forward_and_generate_against_oracle():
     assert agree >= 8, (got, ref_toks)
     # twice: the graphs are replayed, the cache is reset by generate
     assert dec.generate(prompt, 12) == got
+    # steps that would consume position max_seq are refused before any launch
+    from alveare_b200._lib import AlvError
+    dec.start(prompt)
+    with pytest.raises(AlvError):
+        dec.run(len(prompt), cfg.max_seq - len(prompt) + 1)
+    dec.run(len(prompt) - 1, cfg.max_seq - len(prompt) - 1)
+    with pytest.raises(AlvError):
+        dec.run(0, 3)
+    dec.run(0, 2)   # positions max_seq - 2 and max_seq - 1
+    with pytest.raises(AlvError):
+        dec.prefill(cfg.max_seq - 3, 4)
+    dec.prefill(0, 4)
+    dec.run(0, cfg.max_seq - 4)
+    with pytest.raises(AlvError):
+        dec.run(1, 0)
+    assert dec.generate(prompt, 12) == got
     dec.free()
 
 
