@@ -2,6 +2,7 @@
 Llama CPU path.
 
     ALVEARE_REFERENCE=/path/to/alveare python tests/golden/make_llama_golden.py [--steps 256]
+    ALVEARE_REFERENCE=/path/to/alveare python tests/golden/make_llama_golden.py --small
 
 Builds the random-init Q4 Llama-3.2-1B-shaped model of BASELINE config 3
 (``oracle.llama.synthetic_weights``, seed 0, quantized with the reference's
@@ -19,6 +20,12 @@ two must agree bit for bit (tokens and every step's logits).  Writes
 ``tests/golden/llama_config3.json``: the prompt, the greedy tokens, each
 step's top-two logits and logits hash, and sha256 digests of the packed
 weights, so a GPU test can rebuild the same model and check it.
+
+``--small`` runs the reference's greedy loop on small models of the same
+family (SMALL_CASES: other FFN widths, vocabularies and prompts) and
+writes ``tests/golden/llama_small.npz`` with every step's full bf16 logits,
+so the CPU test suite checks the numpy restatement against the reference
+itself in seconds.
 """
 from __future__ import annotations
 
@@ -40,6 +47,18 @@ sys.path.insert(0, str(ROOT))
 from oracle import llama  # noqa: E402
 
 OUT = Path(__file__).resolve().parent / "llama_config3.json"
+OUT_SMALL = Path(__file__).resolve().parent / "llama_small.npz"
+
+# Small models for the CPU-side pin of oracle/llama.py: (name, Config
+# arguments, weight seed, prompt length, greedy steps).  The reference's CPU
+# path fixes the Llama-3.2-1B attention shapes and depth (runtime/py/
+# model.py:821-837, 921: 16 layers, 32 query heads and 8 KV heads of 64,
+# hidden 2048), so the cases vary the FFN width, the vocabulary and the
+# prompt length around them.
+SMALL_CASES = (
+    ("i512_v1024", dict(intermediate=512, vocab=1024, vocab_padded=1024, max_seq=64), 11, 24, 16),
+    ("i1536_v2048", dict(intermediate=1536, vocab=2048, vocab_padded=2048, max_seq=64), 5, 40, 12),
+)
 
 
 def _reference_root() -> Path:
@@ -144,12 +163,48 @@ def weights_digest(w: dict, cfg: llama.Config) -> dict:
     return out
 
 
+def bf16_bits(a) -> np.ndarray:
+    return np.asarray(a, np.float32).astype(bfloat16).view(np.uint16)
+
+
+def make_small(ref: Path):
+    """The reference's greedy loop on each of SMALL_CASES; every step's full
+    logits (bf16 bits) into llama_small.npz, after checking that the numpy
+    restatement gives the same bits."""
+    cls = load_reference_model_class(ref)
+    quantize = reference_quantizer(ref)
+    out = {}
+    for name, kw, seed, n_prompt, steps in SMALL_CASES:
+        cfg = llama.Config(**kw)
+        w, prompt = llama.synthetic_weights(cfg, seed, quantize=quantize)
+        prompt = prompt[:n_prompt]
+        m = build_reference_model(cls, cfg, w, ref)
+        toks, logits = reference_generate(m, prompt, steps)
+        o_toks, o_logits = llama.LlamaOracle(cfg, w).generate(prompt, steps, keep_logits=True)
+        agree = o_toks == toks and all(np.array_equal(bf16_bits(a), bf16_bits(b)) for a, b in zip(o_logits, logits))
+        print(f"{name}: tokens {toks}; oracle agrees: {agree}")
+        if not agree:
+            raise SystemExit(f"{name}: the restatement differs from the reference")
+        out[f"{name}.config"] = np.array(json.dumps(kw))
+        out[f"{name}.seed"] = np.array(seed)
+        out[f"{name}.prompt"] = np.asarray(prompt, np.int64)
+        out[f"{name}.tokens"] = np.asarray(toks, np.int64)
+        out[f"{name}.logits_bf16"] = np.stack([bf16_bits(lg) for lg in logits])
+        out[f"{name}.weights_sha256"] = np.array(json.dumps(weights_digest(w, cfg)))
+    np.savez_compressed(OUT_SMALL, **out)
+    print(f"wrote {OUT_SMALL}")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--small", action="store_true", help="write llama_small.npz (SMALL_CASES) instead")
     args = ap.parse_args()
     ref = _reference_root()
+    if args.small:
+        make_small(ref)
+        return
     cfg = llama.Config(max_seq=512)
     t0 = time.time()
     w, prompt = llama.synthetic_weights(cfg, args.seed, quantize=reference_quantizer(ref))
