@@ -15,15 +15,17 @@ numpy arrays (synchronous copy in / copy out, like the reference's
 ``_sync_to_device``).  ``m``, ``k_tile`` and ``m_I`` are NPU tiling knobs;
 they are accepted and ignored.  A raw ``W_combined`` buffer is repacked into
 the GPU layout on its first use and the resident copy is reused while the
-same buffer (same object, address and size, and for a torch tensor the same
-version counter) comes back, the way the reference keeps its weights resident
+same buffer (same object, address and size; for a torch tensor the same
+version counter, for a host array the same fingerprint of 4 KB sampled over
+it) comes back, the way the reference keeps its weights resident
 (model.py:41-53); :class:`Q4Weight` registers one explicitly, and
 :func:`clear_weight_cache` drops the cached copies (call it after changing a
-raw buffer in place by other means than torch).
+few bytes of a host array, or a tensor by other means than torch).
 """
 from __future__ import annotations
 
 import ctypes
+import zlib
 from dataclasses import dataclass
 
 import numpy as np
@@ -257,7 +259,18 @@ def _buffer_key(W, N: int, K: int, device):
         dev = W.device.index if W.is_cuda else -1
         return ("torch", dev, W.data_ptr(), W.numel() * W.element_size(), N, K, device), W._version
     a = np.asarray(W)
-    return ("host", -1, a.__array_interface__["data"][0], a.nbytes, N, K, device), 0
+    return ("host", -1, a.__array_interface__["data"][0], a.nbytes, N, K, device), _host_fingerprint(a)
+
+
+def _host_fingerprint(a: np.ndarray) -> int:
+    """crc32 of 64 windows of 64 bytes spread evenly over a host buffer (all
+    of it up to 4 KB): a staging buffer refilled with another matrix gets a
+    new fingerprint, so it is repacked again, without reading it whole."""
+    b = np.ascontiguousarray(a).reshape(-1).view(np.uint8)
+    if b.size <= 4096:
+        return zlib.crc32(b.tobytes())
+    starts = np.linspace(0, b.size - 64, 64).astype(np.int64)
+    return zlib.crc32(b[(starts[:, None] + np.arange(64)).reshape(-1)].tobytes())
 
 
 def clear_weight_cache() -> None:
