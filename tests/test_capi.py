@@ -49,6 +49,19 @@ def test_version_and_null_handling(lib):
     assert lib.alv_ctx_create(0, None) == 1
 
 
+def test_every_entry_point_rejects_a_null_context(lib):
+    """Every function taking a context returns ALV_ERR_ARG for a null one
+    (all other arguments zero or null), before touching anything."""
+    checked = 0
+    for name, (_, args) in _lib.SIGNATURES.items():
+        if not args or args[0] is not ctypes.c_void_p or name == "alv_last_error":
+            continue
+        vals = [0 if a in (ctypes.c_int, ctypes.c_uint32, ctypes.c_int64, ctypes.c_size_t) else None for a in args]
+        assert getattr(lib, name)(*vals) == 1, name
+        checked += 1
+    assert checked >= 30
+
+
 def test_no_device_is_reported_not_crashed(lib):
     torch = pytest.importorskip("torch")
     if torch.cuda.is_available():
